@@ -1,0 +1,119 @@
+/*
+ * torchbvh_b200 C ABI: the drop-in boundary of the B200 BVH k-NN path.
+ *
+ * Plain pointers and sizes only. Every device pointer must live on `device`;
+ * every call enqueues work on `stream` (a cudaStream_t passed as void*) and
+ * returns without synchronising. Outputs and workspace are caller-allocated
+ * (the Python layer uses the PyTorch caching allocator). Return value 0 is
+ * success; otherwise one of TBVH_ERR_* with a message in tbvh_last_error().
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * the torchbvh 0.3.4 project).
+ */
+#ifndef TORCHBVH_B200_H_
+#define TORCHBVH_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TBVH_OK = 0,
+  TBVH_ERR_BAD_ARG = 1,        /* shape / pointer / size validation (reference: TORCH_CHECK) */
+  TBVH_ERR_UNSUPPORTED_K = 2,  /* k not in {4, 8, 16, 32} */
+  TBVH_ERR_CUDA = 3,           /* CUDA launch or runtime error */
+  TBVH_ERR_WORKSPACE = 4       /* workspace smaller than the *_workspace_size() answer */
+};
+
+/* Device status bits, reported by tbvh_device_status(). */
+enum {
+  TBVH_DEVICE_LOOKBACK_TIMEOUT = 1, /* a radix-sort look-back wait hit its bound */
+  TBVH_DEVICE_STACK_OVERFLOW = 2,   /* traversal stack guard tripped */
+  TBVH_DEVICE_TREE_COUNTER = 4,     /* tree-build arrival counter out of range */
+  TBVH_DEVICE_BAD_INDEX = 8         /* an index read from device memory was out of range (clamped) */
+};
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* tbvh_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+int tbvh_abi_version(void);
+
+/* Reads (and optionally clears) the error bits kernels raised on `device`
+ * instead of hanging. Synchronous. No reference counterpart (the reference
+ * waits without bounds inside CUB). */
+int tbvh_device_status(int device, unsigned* out_bits, int clear);
+
+/* Number of kernels this library has launched in this process (all devices).
+ * Host-side counter; lets callers attribute launches to this library. */
+uint64_t tbvh_kernel_launch_count(void);
+
+/* Real node count 2N - 1 + popcount(2^ceil(log2 N) - N) of one cloud
+ * (torchbvh/csrc/implicit_tree.cuh:61-64). */
+int64_t tbvh_real_node_count(int64_t num_points);
+
+/* ---------------------------------------------------------------------------
+ * BVH build. Replaces build_bvh_batched_cooperative_cuda
+ * (torchbvh/csrc/bvh_build.cu:679-721, bound as build_bvh_batched_cooperative
+ * in torchbvh/csrc/bindings.cpp:155-157,192) and, for ragged input, the
+ * per-sample Python loop of _build_bvh_ragged (torchbvh/_query.py:68-85).
+ *
+ * Clouds: fixed size when points_per_cloud > 0 (points is (B, N, D)), else
+ * ragged with offsets (B + 1 int64, both a device copy and a host copy).
+ * Outputs, packed by cloud:
+ *   node_aabbs      float32 [sum_b nr_b, 2*dim]  rows [lo.., hi..], implicit memory order
+ *   sorted_indices  int64   [sum_b N_b]          local (in-cloud) point index per sorted leaf
+ *   scene_min/max   float32 [B, dim]
+ *   left_child_mem / right_child_mem / mem_to_leaf  int32, nullable (all three or none);
+ *                   one shared set of nr entries when traversal_arrays_per_cloud == 0
+ *                   (fixed-size batches), else packed per cloud.
+ */
+size_t tbvh_build_workspace_size(int64_t num_clouds, int64_t points_per_cloud,
+                                 const int64_t* offsets_host, int dim);
+int tbvh_build(int device, const float* points, int64_t num_clouds, int64_t points_per_cloud,
+               const int64_t* offsets_dev, const int64_t* offsets_host, int dim,
+               float* node_aabbs, int64_t* sorted_indices, float* scene_min, float* scene_max,
+               int32_t* left_child_mem, int32_t* right_child_mem, int32_t* mem_to_leaf,
+               int traversal_arrays_per_cloud,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Morton permutation of query points. Replaces morton_sort_queries_narrow_cuda
+ * (torchbvh/csrc/morton_sort.cu:264-287, bound as morton_sort_queries_narrow in
+ * torchbvh/csrc/bindings.cpp:197). order_out[p] is the local query index of
+ * the p-th query of its cloud in (Morton code, index) order, codes taken
+ * against that cloud's scene_min/scene_max.
+ */
+size_t tbvh_sort_queries_workspace_size(int64_t num_clouds, int64_t total_queries, int dim);
+int tbvh_sort_queries(int device, const float* queries, int64_t num_clouds, int64_t queries_per_cloud,
+                      const int64_t* query_offsets_dev, int64_t total_queries, int dim,
+                      const float* scene_min, const float* scene_max, int64_t* order_out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Exact k-NN. Replaces query_knn_batched_cached_bounds_cuda and
+ * query_knn_batched_cached_bounds_ordered_cuda (torchbvh/csrc/knn_query.cu:
+ * 419-446, bound in torchbvh/csrc/bindings.cpp:198-199) and, for ragged
+ * input, the per-sample loop of _query_knn_ragged (torchbvh/_query.py:299-366).
+ * order may be NULL (identity order, the unordered reference kernel).
+ * Outputs: out_indices int64 [total_queries, k] (local source indices),
+ * out_distances float32 [total_queries, k], ascending, at the query's row.
+ * k in {4, 8, 16, 32}; every cloud must hold at least k points.
+ */
+size_t tbvh_query_knn_workspace_size(int64_t num_clouds, int64_t points_per_cloud);
+int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                   int64_t num_clouds, int64_t points_per_cloud,
+                   const int64_t* point_offsets_dev, const int64_t* point_offsets_host,
+                   const float* queries, int64_t queries_per_cloud, const int64_t* query_offsets_dev,
+                   int64_t total_queries, const int64_t* order, int dim, int k,
+                   int64_t* out_indices, float* out_distances,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TORCHBVH_B200_H_ */

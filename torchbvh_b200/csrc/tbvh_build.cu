@@ -1,0 +1,971 @@
+// BVH build for the B200 k-NN path: per-cloud scene bounds, Morton keys with
+// fused digit histograms, a stable onesweep LSD radix sort (8-bit digits,
+// decoupled look-back with bounded waits) and the implicit-tree AABB build.
+//
+// Replaces, for the k-NN path, torchbvh/csrc/bvh_build.cu:453-721 (bounds,
+// Morton keys, CUB segmented sort, lower/upper AABB build, traversal arrays)
+// and torchbvh/csrc/morton_sort.cu:43-81,212-287 (query Morton permutation).
+// Fixed-size batches and ragged batches share one launch sequence; the cloud
+// id enters the sort as the most significant digits of a composite key, so
+// every cloud is sorted independently and stably by (Morton code, index).
+#include <atomic>
+#include <cstdio>
+
+#include "tbvh_kernels.h"
+
+namespace tbvh {
+
+// Per-device status word. Kernels OR error bits into it instead of hanging or
+// trapping; the host reads it with tbvh_device_status().
+__device__ unsigned g_tbvh_status;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+unsigned* g_status_ptr[kMaxDevices] = {};
+
+__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
+
+// Exclusive scan of one value per thread over a 256-thread block. `s_warp`
+// needs 8 entries. Returns the exclusive prefix; `total` gets the block sum.
+template <typename T>
+__device__ __forceinline__ T block_exclusive_scan_256(T v, T* s_warp, T& total) {
+  const unsigned lane = lane_id();
+  const unsigned warp = threadIdx.x >> 5;
+  T x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= unsigned(o)) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    T w = lane < 8 ? s_warp[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const T y = __shfl_up_sync(kFullMask, w, o);
+      if (lane >= unsigned(o)) w += y;
+    }
+    if (lane < 8) s_warp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  total = s_warp[7];
+  const T before = warp == 0 ? T(0) : s_warp[warp - 1];
+  const T result = before + x - v;
+  __syncthreads();  // s_warp may be reused by the caller
+  return result;
+}
+
+__device__ __forceinline__ uint32_t composite_digit(uint32_t key, uint32_t cloud, int code_bits, int lo_bit) {
+  const uint64_t comp = (uint64_t(cloud) << code_bits) | uint64_t(key);
+  return uint32_t(comp >> lo_bit) & 0xffu;
+}
+
+__device__ __forceinline__ void device_error(unsigned* status, unsigned bits) {
+  if (status) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------------------
+// Per-cloud tree facts (device side of cloud_tree_facts()).
+// ---------------------------------------------------------------------------
+__host__ __device__ inline CloudTree tree_facts(int64_t n) {
+  CloudTree t{};
+  t.n = n;
+  t.leaf_level = n > 0 ? ceil_log2_i64(n) : 0;
+  t.sub_level = t.leaf_level > kTreeSubLevels ? t.leaf_level - kTreeSubLevels : 0;
+  return t;
+}
+
+__host__ __device__ inline int64_t tree_blocks_of(const CloudTree& t) {
+  return t.n > 0 ? level_count(t.n, t.leaf_level, t.sub_level) : 0;
+}
+
+__host__ __device__ inline int64_t tree_counters_of(const CloudTree& t) {
+  int64_t total = 0;
+  int lv = t.sub_level;
+  while (lv > 0) {
+    const int lam = lv > kTreeHopLevels ? lv - kTreeHopLevels : 0;
+    total += level_count(t.n, t.leaf_level, lam);
+    lv = lam;
+  }
+  return total;
+}
+
+// ---------------------------------------------------------------------------
+// Init: zero scratch ranges, seed the bounds reduction and (ragged) compute
+// the per-cloud table with a block scan in block 0.
+// ---------------------------------------------------------------------------
+struct ZeroRange {
+  uint32_t* ptr;
+  int64_t words;
+};
+
+struct InitArgs {
+  ZeroRange zero[4];
+  uint32_t* bounds_enc;  // nullable
+  int bounds_words;      // num_clouds * 2D
+  int dim;
+  CloudMap clouds;
+  CloudTree* table;      // nullable
+};
+
+__global__ void __launch_bounds__(256) k_init(InitArgs a) {
+  const int64_t gtid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t gstride = int64_t(gridDim.x) * blockDim.x;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    uint32_t* p = a.zero[r].ptr;
+    const int64_t words = a.zero[r].words;
+    if (p == nullptr) continue;
+    for (int64_t i = gtid; i < words; i += gstride) p[i] = 0u;
+  }
+  if (a.bounds_enc) {
+    const uint32_t enc_lo = float_to_ordered(1.0e30f);
+    const uint32_t enc_hi = float_to_ordered(-1.0e30f);
+    for (int64_t i = gtid; i < a.bounds_words; i += gstride) {
+      const int within = int(i % (2 * a.dim));
+      a.bounds_enc[i] = within < a.dim ? enc_lo : enc_hi;
+    }
+  }
+  if (a.table && blockIdx.x == 0) {
+    __shared__ int64_t s_warp[8];
+    int64_t carry_rows = 0, carry_blocks = 0, carry_ctr = 0;
+    for (int base = 0; base < a.clouds.num_clouds; base += 256) {
+      const int b = base + int(threadIdx.x);
+      const bool valid = b < a.clouds.num_clouds;
+      const int64_t n = valid ? a.clouds.size(b) : 0;
+      CloudTree t = tree_facts(n);
+      const int64_t rows = n > 0 ? real_node_count(n) : 0;
+      const int64_t blocks = tree_blocks_of(t);
+      const int64_t ctrs = n > 0 ? tree_counters_of(t) : 0;
+      int64_t tot_rows, tot_blocks, tot_ctrs;
+      const int64_t ex_rows = block_exclusive_scan_256<int64_t>(rows, s_warp, tot_rows);
+      const int64_t ex_blocks = block_exclusive_scan_256<int64_t>(blocks, s_warp, tot_blocks);
+      const int64_t ex_ctrs = block_exclusive_scan_256<int64_t>(ctrs, s_warp, tot_ctrs);
+      if (valid) {
+        t.row_off = carry_rows + ex_rows;
+        t.tree_cta = carry_blocks + ex_blocks;
+        t.counter = carry_ctr + ex_ctrs;
+        a.table[b] = t;
+      }
+      carry_rows += tot_rows;
+      carry_blocks += tot_blocks;
+      carry_ctr += tot_ctrs;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Scene bounds: every block reduces a contiguous chunk; per-thread running
+// boxes are flushed on cloud changes, combined per warp and per block, then
+// merged into the per-cloud result with order-preserving atomics. Seeds and
+// min/max semantics follow torchbvh/csrc/bvh_build.cu:453-494.
+// ---------------------------------------------------------------------------
+template <int D>
+__device__ __forceinline__ void flush_box(uint32_t* enc, int cloud, const float* lo, const float* hi) {
+#pragma unroll
+  for (int a = 0; a < D; ++a) {
+    atomicMin(enc + cloud * 2 * D + a, float_to_ordered(lo[a]));
+    atomicMax(enc + cloud * 2 * D + D + a, float_to_ordered(hi[a]));
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) k_bounds(const float* __restrict__ pts, CloudMap cm, int64_t n,
+                                                int64_t chunk, uint32_t* __restrict__ enc) {
+  __shared__ int s_cloud[8];
+  __shared__ float s_box[8][2 * D];
+  const int64_t begin = int64_t(blockIdx.x) * chunk;
+  const int64_t end = begin + chunk < n ? begin + chunk : n;
+  int cur = -1;
+  int64_t cur_end = -1;
+  float lo[D], hi[D];
+#pragma unroll
+  for (int a = 0; a < D; ++a) { lo[a] = 1.0e30f; hi[a] = -1.0e30f; }
+  for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    if (i >= cur_end) {
+      const int c = cm.find(i);
+      if (cur >= 0 && c != cur) {
+        flush_box<D>(enc, cur, lo, hi);
+#pragma unroll
+        for (int a = 0; a < D; ++a) { lo[a] = 1.0e30f; hi[a] = -1.0e30f; }
+      }
+      cur = c;
+      cur_end = cm.start(c) + cm.size(c);
+    }
+#pragma unroll
+    for (int a = 0; a < D; ++a) {
+      const float v = pts[i * D + a];
+      lo[a] = fminf(lo[a], v);
+      hi[a] = fmaxf(hi[a], v);
+    }
+  }
+  const unsigned lane = lane_id();
+  const unsigned warp = threadIdx.x >> 5;
+  const int c0 = __shfl_sync(kFullMask, cur, 0);
+  // Threads without elements (cur == -1) carry the neutral box.
+  const bool uniform = __all_sync(kFullMask, cur == c0 || cur == -1);
+  int wc = __reduce_max_sync(kFullMask, uniform ? (cur < 0 ? -1 : cur) : -1);
+  if (uniform) {
+#pragma unroll
+    for (int a = 0; a < D; ++a) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        lo[a] = fminf(lo[a], __shfl_xor_sync(kFullMask, lo[a], o));
+        hi[a] = fmaxf(hi[a], __shfl_xor_sync(kFullMask, hi[a], o));
+      }
+    }
+    if (lane == 0) {
+      s_cloud[warp] = wc;
+#pragma unroll
+      for (int a = 0; a < D; ++a) { s_box[warp][a] = lo[a]; s_box[warp][D + a] = hi[a]; }
+    }
+  } else {
+    if (cur >= 0) flush_box<D>(enc, cur, lo, hi);
+    if (lane == 0) s_cloud[warp] = -1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc_cloud = -1;
+    float alo[D], ahi[D];
+    for (int w = 0; w < 8; ++w) {
+      const int c = s_cloud[w];
+      if (c < 0) continue;
+      if (c != acc_cloud) {
+        if (acc_cloud >= 0) flush_box<D>(enc, acc_cloud, alo, ahi);
+        acc_cloud = c;
+#pragma unroll
+        for (int a = 0; a < D; ++a) { alo[a] = s_box[w][a]; ahi[a] = s_box[w][D + a]; }
+      } else {
+#pragma unroll
+        for (int a = 0; a < D; ++a) {
+          alo[a] = fminf(alo[a], s_box[w][a]);
+          ahi[a] = fmaxf(ahi[a], s_box[w][D + a]);
+        }
+      }
+    }
+    if (acc_cloud >= 0) flush_box<D>(enc, acc_cloud, alo, ahi);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Morton keys + digit histograms for every sort pass (one read of the
+// coordinates). Histograms are aggregated per warp with match_any, per block
+// in shared memory, then added to the global per-pass histograms.
+// ---------------------------------------------------------------------------
+template <int D, bool kEncodedBounds>
+__global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, CloudMap cm, int64_t n,
+                                              const uint32_t* __restrict__ enc,
+                                              const float* __restrict__ smin, const float* __restrict__ smax,
+                                              uint32_t* __restrict__ keys, uint32_t* __restrict__ hist,
+                                              int code_bits, int passes,
+                                              float* __restrict__ out_min, float* __restrict__ out_max) {
+  __shared__ uint32_t s_hist[kMaxSortPasses][kRadix];
+  for (int i = threadIdx.x; i < kMaxSortPasses * kRadix; i += blockDim.x) (&s_hist[0][0])[i] = 0u;
+  if (kEncodedBounds && blockIdx.x == 0) {
+    const int words = cm.num_clouds * D;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const int b = i / D, a = i % D;
+      out_min[i] = ordered_to_float(enc[b * 2 * D + a]);
+      out_max[i] = ordered_to_float(enc[b * 2 * D + D + a]);
+    }
+  }
+  __syncthreads();
+  const unsigned lane = lane_id();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int64_t rounds = (n + int64_t(gridDim.x) * blockDim.x - 1) / (int64_t(gridDim.x) * blockDim.x);
+  int cur = -1;
+  int64_t cur_end = -1;
+  float lo[D], hi[D];
+  for (int64_t r = 0; r < rounds; ++r) {
+    const int64_t i = (r * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
+    const bool valid = i < n;
+    uint32_t code = 0;
+    int c = 0;
+    if (valid) {
+      if (i >= cur_end || cur < 0) {
+        cur = cm.find(i);
+        cur_end = cm.start(cur) + cm.size(cur);
+#pragma unroll
+        for (int a = 0; a < D; ++a) {
+          if (kEncodedBounds) {
+            lo[a] = ordered_to_float(enc[cur * 2 * D + a]);
+            hi[a] = ordered_to_float(enc[cur * 2 * D + D + a]);
+          } else {
+            lo[a] = smin[cur * D + a];
+            hi[a] = smax[cur * D + a];
+          }
+        }
+      }
+      c = cur;
+      float p[D];
+#pragma unroll
+      for (int a = 0; a < D; ++a) p[a] = pts[i * D + a];
+      code = morton_code<D>(p, lo, hi);
+      keys[i] = code;
+    }
+    for (int ps = 0; ps < passes; ++ps) {
+      const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
+      const unsigned peers = __match_any_sync(kFullMask, d);
+      if (d < 0x100u && (peers & lt_mask) == 0u) atomicAdd(&s_hist[ps][d], uint32_t(__popc(peers)));
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * kRadix; i += blockDim.x) {
+    const uint32_t v = (&s_hist[0][0])[i];
+    if (v) atomicAdd(hist + i, v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One stable LSD pass over composite-key bits [lo_bit, lo_bit + 8).
+//
+// Tiles are claimed in launch order through an atomic ticket, so a tile only
+// ever waits on tiles owned by blocks that are already running: the look-back
+// makes progress without co-residency assumptions. Every wait is bounded; on
+// expiry the kernel records kDevErrLookbackTimeout and carries on.
+// ---------------------------------------------------------------------------
+constexpr uint64_t kLbAggregate = 1ull << 62;
+constexpr uint64_t kLbPrefix = 2ull << 62;
+constexpr uint64_t kLbFlags = 3ull << 62;
+constexpr int kLbSpinLimit = 1 << 22;
+
+struct PassArgs {
+  const uint32_t* keys_in;
+  const uint32_t* vals_in;  // nullptr: value = element index
+  uint32_t* keys_out;
+  uint32_t* vals_out;
+  int64_t* final_out;       // last pass: local (in-cloud) index as int64
+  const uint32_t* hist;     // 256 counts for this pass
+  uint64_t* lookback;       // this pass: tiles x 256
+  uint64_t* lookback_next;  // next pass: tiles x 256 (cleared here), nullable
+  uint32_t* tile_ctr;
+  int64_t n;
+  int lo_bit;
+  int code_bits;
+  int needs_cloud;
+  CloudMap cm;
+  unsigned* status;
+};
+
+struct PassSmem {
+  uint32_t keys[kSortTile];
+  uint32_t vals[kSortTile];
+  uint8_t dig[kSortTile];
+  uint16_t whist[kSortThreads / 32][kRadix];
+  uint32_t local_start[kRadix];
+  int64_t gbase[kRadix];
+  uint32_t scan_warp[8];
+  int64_t scan_warp64[8];
+  uint32_t tile;
+};
+
+__global__ void __launch_bounds__(kSortThreads) k_sort_pass(PassArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  PassSmem& s = *reinterpret_cast<PassSmem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const unsigned lane = lane_id();
+  const unsigned warp = threadIdx.x >> 5;
+  const unsigned lt_mask = (1u << lane) - 1u;
+
+  if (tid == 0) s.tile = atomicAdd(a.tile_ctr, 1u);
+  for (int i = tid; i < (kSortThreads / 32) * kRadix; i += kSortThreads) (&s.whist[0][0])[i] = 0;
+  // Global exclusive bin bases for this pass.
+  uint32_t total_unused;
+  const uint32_t bin_base = block_exclusive_scan_256<uint32_t>(a.hist[tid], s.scan_warp, total_unused);
+  // (block_exclusive_scan_256 ends with __syncthreads, so s.tile / s.whist are visible.)
+  const int64_t tile = s.tile;
+  const int64_t tile_start = tile * kSortTile;
+  const int tile_n = int(a.n - tile_start < kSortTile ? a.n - tile_start : kSortTile);
+  if (a.lookback_next) a.lookback_next[tile * kRadix + tid] = 0ull;
+
+  uint32_t key[kSortIpt], val[kSortIpt], packed[kSortIpt];  // packed = rank << 9 | digit
+#pragma unroll
+  for (int r = 0; r < kSortIpt; ++r) {
+    const int idx = int(warp) * 32 * kSortIpt + r * 32 + int(lane);
+    const bool valid = idx < tile_n;
+    const int64_t e = tile_start + idx;
+    key[r] = valid ? a.keys_in[e] : 0u;
+    val[r] = valid ? (a.vals_in ? a.vals_in[e] : uint32_t(e)) : 0u;
+  }
+#pragma unroll
+  for (int r = 0; r < kSortIpt; ++r) {
+    const int idx = int(warp) * 32 * kSortIpt + r * 32 + int(lane);
+    const bool valid = idx < tile_n;
+    uint32_t d = 0x100u;
+    if (valid) {
+      const uint32_t cloud = a.needs_cloud ? uint32_t(a.cm.find(int64_t(val[r]))) : 0u;
+      d = composite_digit(key[r], cloud, a.code_bits, a.lo_bit);
+    }
+    const unsigned peers = __match_any_sync(kFullMask, d);
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (int(lane) == leader && d < 0x100u) {
+      base = s.whist[warp][d];
+      s.whist[warp][d] = uint16_t(base + __popc(peers));
+    }
+    base = __shfl_sync(kFullMask, base, leader);
+    packed[r] = ((base + __popc(peers & lt_mask)) << 9) | d;
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Per-digit: exclusive prefix over warps, tile count.
+  const int d = tid;
+  uint32_t run = 0;
+#pragma unroll
+  for (int w = 0; w < kSortThreads / 32; ++w) {
+    const uint32_t c = s.whist[w][d];
+    s.whist[w][d] = uint16_t(run);
+    run += c;
+  }
+  const uint32_t tile_cnt = run;
+  volatile uint64_t* lb = reinterpret_cast<volatile uint64_t*>(a.lookback);
+  if (tile == 0) {
+    lb[d] = kLbPrefix | uint64_t(tile_cnt);
+  } else {
+    lb[tile * kRadix + d] = kLbAggregate | uint64_t(tile_cnt);
+  }
+  int64_t excl = 0;
+  if (tile > 0) {
+    int64_t t = tile - 1;
+    int spins = 0;
+    while (t >= 0) {
+      const uint64_t v = lb[t * kRadix + d];
+      const uint64_t flag = v & kLbFlags;
+      if (flag == 0) {
+        if (++spins > kLbSpinLimit) {
+          device_error(a.status, kDevErrLookbackTimeout);
+          break;
+        }
+        if (spins > 64) __nanosleep(32);
+        continue;
+      }
+      excl += int64_t(v & 0xffffffffull);
+      if (flag == kLbPrefix) break;
+      --t;
+    }
+    lb[tile * kRadix + d] = kLbPrefix | uint64_t(excl + tile_cnt);
+  }
+  uint32_t tile_total;
+  const uint32_t local_start = block_exclusive_scan_256<uint32_t>(tile_cnt, s.scan_warp, tile_total);
+  s.local_start[d] = local_start;
+  s.gbase[d] = int64_t(bin_base) + excl - int64_t(local_start);
+  __syncthreads();
+
+  // Scatter into shared memory in digit order (stable within each digit).
+#pragma unroll
+  for (int r = 0; r < kSortIpt; ++r) {
+    const uint32_t dg = packed[r] & 0x1ffu;
+    if (dg < 0x100u) {
+      const uint32_t lp = s.local_start[dg] + s.whist[warp][dg] + (packed[r] >> 9);
+      s.keys[lp] = key[r];
+      s.vals[lp] = val[r];
+      s.dig[lp] = uint8_t(dg);
+    }
+  }
+  __syncthreads();
+
+  // Write out: consecutive shared slots of one digit land on consecutive
+  // global positions, so the stores coalesce into runs.
+  // The range checks only matter if an earlier pass gave up a bounded wait
+  // (status bit set): they keep a corrupted permutation from writing out of bounds.
+  if (a.final_out) {
+    for (int i = tid; i < tile_n; i += kSortThreads) {
+      const int64_t g = s.gbase[s.dig[i]] + i;
+      const uint32_t v = s.vals[i];
+      const int c = a.cm.find(int64_t(v));
+      if (g >= 0 && g < a.n) a.final_out[g] = int64_t(v) - a.cm.start(c);
+    }
+  } else {
+    for (int i = tid; i < tile_n; i += kSortThreads) {
+      const int64_t g = s.gbase[s.dig[i]] + i;
+      if (g >= 0 && g < a.n) {
+        a.keys_out[g] = s.keys[i];
+        a.vals_out[g] = s.vals[i];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Implicit-tree AABB build.
+//
+// Block (cloud, js) owns the subtree rooted at level Ls = max(L - 10, 0),
+// index js: it gathers its <= 1024 sorted points, writes the leaf rows and
+// merges upward (4 leaves per thread, then warp shuffles, then across warps),
+// writing every real node row. Upper levels are merged in hops of 8 levels:
+// the last block to finish inside a hop group (atomic ticket after a
+// __threadfence) merges that group, exactly once. Node rows are written in
+// the reference's memory order (level-major over real nodes) together with
+// left_child_mem / right_child_mem / mem_to_leaf (bvh_build.cu:361-398).
+// ---------------------------------------------------------------------------
+struct TreeArgs {
+  const float* points;
+  const int64_t* sorted;
+  float* node_aabbs;
+  int32_t* left;
+  int32_t* right;
+  int32_t* m2l;
+  int arrays_per_cloud;
+  CloudMap cm;
+  const CloudTree* table;  // ragged
+  CloudTree uni;           // uniform clouds
+  int64_t uni_blocks;      // blocks per uniform cloud
+  int64_t uni_rows;        // rows per uniform cloud
+  int64_t uni_counters;    // counters per uniform cloud
+  uint32_t* counters;
+  unsigned* status;
+};
+
+template <int D>
+struct TreeCtx {
+  const TreeArgs* a;
+  const int64_t* cnt;     // shared, per level
+  const int64_t* rowoff;  // shared, per level
+  float* rows;            // cloud's first row
+  int32_t* left;          // nullable, cloud's first entry
+  int32_t* right;
+  int32_t* m2l;
+  int L;
+
+  __device__ __forceinline__ void emit(int level, int64_t j, const float* lo, const float* hi) const {
+    const int64_t row = rowoff[level] + j;
+    float* r = rows + row * (2 * D);
+    if constexpr (D == 3) {
+      reinterpret_cast<float2*>(r)[0] = make_float2(lo[0], lo[1]);
+      reinterpret_cast<float2*>(r)[1] = make_float2(lo[2], hi[0]);
+      reinterpret_cast<float2*>(r)[2] = make_float2(hi[1], hi[2]);
+    } else {
+      reinterpret_cast<float4*>(r)[0] = make_float4(lo[0], lo[1], hi[0], hi[1]);
+    }
+    if (left) {
+      if (level == L) {
+        left[row] = -1;
+        right[row] = -1;
+        m2l[row] = int32_t(j);
+      } else {
+        const int64_t c0 = 2 * j;
+        left[row] = int32_t(rowoff[level + 1] + c0);
+        right[row] = c0 + 1 < cnt[level + 1] ? int32_t(rowoff[level + 1] + c0 + 1) : -1;
+        m2l[row] = -1;
+      }
+    }
+  }
+};
+
+template <int D>
+__device__ __forceinline__ void merge_box(float* lo, float* hi, const float* olo, const float* ohi) {
+#pragma unroll
+  for (int a = 0; a < D; ++a) { lo[a] = fminf(lo[a], olo[a]); hi[a] = fmaxf(hi[a], ohi[a]); }
+}
+
+template <int D>
+__device__ __forceinline__ void shfl_merge(float* lo, float* hi, int offset) {
+#pragma unroll
+  for (int a = 0; a < D; ++a) {
+    lo[a] = fminf(lo[a], __shfl_down_sync(kFullMask, lo[a], offset));
+    hi[a] = fmaxf(hi[a], __shfl_down_sync(kFullMask, hi[a], offset));
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void load_row_cg(const float* rows, int64_t row, float* lo, float* hi) {
+  const float* r = rows + row * (2 * D);
+#pragma unroll
+  for (int a = 0; a < D; ++a) { lo[a] = __ldcg(r + a); hi[a] = __ldcg(r + D + a); }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTreeThreads) k_tree(TreeArgs a) {
+  __shared__ int64_t s_cnt[34];
+  __shared__ int64_t s_rowoff[34];
+  __shared__ float s_wbox[kTreeThreads / 32][2 * D];
+  __shared__ CloudTree s_t;
+  __shared__ int64_t s_js;
+  __shared__ int64_t s_ptoff;
+  __shared__ int s_cloud;
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x;
+  const unsigned lane = lane_id();
+  const unsigned warp = threadIdx.x >> 5;
+  if (tid == 0) {
+    int b;
+    CloudTree t;
+    int64_t js;
+    if (a.table == nullptr) {
+      b = int(int64_t(blockIdx.x) / a.uni_blocks);
+      js = int64_t(blockIdx.x) - int64_t(b) * a.uni_blocks;
+      t = a.uni;
+      t.row_off = int64_t(b) * a.uni_rows;
+      t.counter = int64_t(b) * a.uni_counters;
+    } else {
+      int lo = 0, hi = a.cm.num_clouds - 1;
+      while (lo < hi) {  // last cloud whose first block <= blockIdx.x (skipping empty tail)
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.table[mid].tree_cta <= int64_t(blockIdx.x)) lo = mid; else hi = mid - 1;
+      }
+      // Clouds own >= 1 block each (n >= 1), so `lo` is the owner.
+      b = lo;
+      t = a.table[b];
+      js = int64_t(blockIdx.x) - t.tree_cta;
+    }
+    s_t = t;
+    s_js = js;
+    s_cloud = b;
+    s_ptoff = a.cm.start(b);
+  }
+  __syncthreads();
+  const CloudTree t = s_t;
+  const int L = t.leaf_level;
+  const int Ls = t.sub_level;
+  const int64_t n = t.n;
+  const int64_t js = s_js;
+  const int64_t pt_off = s_ptoff;
+  if (tid <= L) s_cnt[tid] = level_count(n, L, tid);
+  __syncthreads();
+  if (tid == 0) {
+    int64_t acc = 0;
+    for (int l = 0; l <= L; ++l) { s_rowoff[l] = acc; acc += s_cnt[l]; }
+    s_rowoff[L + 1] = acc;
+  }
+  __syncthreads();
+
+  TreeCtx<D> ctx;
+  ctx.a = &a;
+  ctx.cnt = s_cnt;
+  ctx.rowoff = s_rowoff;
+  ctx.rows = a.node_aabbs + t.row_off * (2 * D);
+  ctx.L = L;
+  const bool write_arrays = a.left != nullptr && (a.arrays_per_cloud || s_cloud == 0);
+  const int64_t arr_base = a.arrays_per_cloud ? t.row_off : 0;
+  ctx.left = write_arrays ? a.left + arr_base : nullptr;
+  ctx.right = write_arrays ? a.right + arr_base : nullptr;
+  ctx.m2l = write_arrays ? a.m2l + arr_base : nullptr;
+
+  const int span = L - Ls;  // levels inside this block's subtree (<= 10)
+  const int64_t base = js << span;
+  const int64_t block_end = base + (int64_t(1) << span);
+  const int64_t limit = block_end < n ? block_end : n;
+  auto present = [&](int level, int64_t j) { return (j << (L - level)) < limit; };
+
+  // Leaves: 4 consecutive sorted positions per thread.
+  float lo4[4][D], hi4[4][D];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int64_t pos = base + 4 * tid + q;
+    if (pos < limit) {
+      int64_t src = a.sorted[pt_off + pos];
+      if (src < 0 || src >= n) {  // only reachable if the sort was corrupted; keep the read in bounds
+        device_error(a.status, kDevErrBadIndex);
+        src = 0;
+      }
+#pragma unroll
+      for (int c = 0; c < D; ++c) {
+        const float v = a.points[(pt_off + src) * D + c];
+        lo4[q][c] = v;
+        hi4[q][c] = v;
+      }
+      ctx.emit(L, pos, lo4[q], hi4[q]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < D; ++c) { lo4[q][c] = INFINITY; hi4[q][c] = -INFINITY; }
+    }
+  }
+  // Level L-1: two nodes per thread.
+  float lo[D], hi[D];
+  float lo2[2][D], hi2[2][D];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int c = 0; c < D; ++c) { lo2[h][c] = lo4[2 * h][c]; hi2[h][c] = hi4[2 * h][c]; }
+    merge_box<D>(lo2[h], hi2[h], lo4[2 * h + 1], hi4[2 * h + 1]);
+    if (L - 1 >= Ls) {
+      const int64_t j = (base >> 1) + 2 * tid + h;
+      if (present(L - 1, j)) ctx.emit(L - 1, j, lo2[h], hi2[h]);
+    }
+  }
+  // Level L-2: one node per thread.
+#pragma unroll
+  for (int c = 0; c < D; ++c) { lo[c] = lo2[0][c]; hi[c] = hi2[0][c]; }
+  merge_box<D>(lo, hi, lo2[1], hi2[1]);
+  if (L - 2 >= Ls) {
+    const int64_t j = (base >> 2) + tid;
+    if (present(L - 2, j)) ctx.emit(L - 2, j, lo, hi);
+  }
+  // Levels L-3 .. L-7 inside the warp.
+#pragma unroll
+  for (int s = 1; s <= 5; ++s) {
+    shfl_merge<D>(lo, hi, 1 << (s - 1));
+    const int level = L - 2 - s;
+    if (level >= Ls && (lane & ((1u << s) - 1u)) == 0u) {
+      const int64_t j = (base >> (2 + s)) + (tid >> s);
+      if (present(level, j)) ctx.emit(level, j, lo, hi);
+    }
+  }
+  // Levels L-8 .. L-10 across the 8 warps.
+  if (lane == 0) {
+#pragma unroll
+    for (int c = 0; c < D; ++c) { s_wbox[warp][c] = lo[c]; s_wbox[warp][D + c] = hi[c]; }
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int c = 0; c < D; ++c) {
+      lo[c] = lane < 8 ? s_wbox[lane][c] : INFINITY;
+      hi[c] = lane < 8 ? s_wbox[lane][D + c] : -INFINITY;
+    }
+#pragma unroll
+    for (int s = 1; s <= 3; ++s) {
+      shfl_merge<D>(lo, hi, 1 << (s - 1));
+      const int level = L - 7 - s;
+      if (level >= Ls && (lane & ((1u << s) - 1u)) == 0u) {
+        const int64_t j = (base >> (7 + s)) + (lane >> s);
+        if (present(level, j)) ctx.emit(level, j, lo, hi);
+      }
+    }
+  }
+  if (Ls == 0) return;
+
+  // Upper levels: hop groups of 8 levels; last arriver merges the group.
+  int lv = Ls;
+  int64_t j = js;
+  int64_t hop_base = 0;
+  while (lv > 0) {
+    const int lam = lv > kTreeHopLevels ? lv - kTreeHopLevels : 0;
+    const int delta = lv - lam;
+    const int64_t g = j >> delta;
+    const int64_t first = g << delta;
+    const int64_t group_end = (g + 1) << delta;
+    const int64_t arrivals = (group_end < s_cnt[lv] ? group_end : s_cnt[lv]) - first;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t old = atomicAdd(a.counters + t.counter + hop_base + g, 1u);
+      if (int64_t(old) >= arrivals) device_error(a.status, kDevErrTreeCounter);
+      s_last = int64_t(old) == arrivals - 1 ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int m = lv - 1; m >= lam; --m) {
+      const int64_t width = int64_t(1) << (m - lam);
+      const int64_t jm = (g << (m - lam)) + tid;
+      if (tid < width && jm < s_cnt[m]) {
+        float clo[D], chi[D];
+        load_row_cg<D>(ctx.rows, s_rowoff[m + 1] + 2 * jm, clo, chi);
+        if (2 * jm + 1 < s_cnt[m + 1]) {
+          float rlo[D], rhi[D];
+          load_row_cg<D>(ctx.rows, s_rowoff[m + 1] + 2 * jm + 1, rlo, rhi);
+          merge_box<D>(clo, chi, rlo, rhi);
+        }
+        ctx.emit(m, jm, clo, chi);
+      }
+      __threadfence();
+      __syncthreads();
+    }
+    hop_base += s_cnt[lam];
+    lv = lam;
+    j = g;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+SortPlan make_sort_plan(int64_t n, int num_clouds, int dim) {
+  SortPlan p;
+  p.n = n;
+  p.code_bits = dim == 3 ? 30 : 32;
+  int cb = 0;
+  while ((int64_t(1) << cb) < num_clouds) ++cb;
+  p.cloud_bits = cb;
+  p.passes = (p.code_bits + p.cloud_bits + 7) / 8;
+  p.tiles = (n + kSortTile - 1) / kSortTile;
+  return p;
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t sort_scratch_bytes(const SortPlan& p) {
+  size_t b = 0;
+  b += 4 * align_up(size_t(p.n) * 4, 256);
+  b += align_up(size_t(kMaxSortPasses) * kRadix * 4, 256);
+  b += align_up(size_t(kMaxSortPasses) * 4, 256);
+  b += 2 * align_up(size_t(p.tiles) * kRadix * 8, 256);
+  return b;
+}
+
+void carve_sort_scratch(const SortPlan& p, char*& cur, SortScratch& s) {
+  auto take = [&](size_t bytes) { char* r = cur; cur += align_up(bytes, 256); return r; };
+  s.keys[0] = reinterpret_cast<uint32_t*>(take(size_t(p.n) * 4));
+  s.keys[1] = reinterpret_cast<uint32_t*>(take(size_t(p.n) * 4));
+  s.vals[0] = reinterpret_cast<uint32_t*>(take(size_t(p.n) * 4));
+  s.vals[1] = reinterpret_cast<uint32_t*>(take(size_t(p.n) * 4));
+  s.hist = reinterpret_cast<uint32_t*>(take(size_t(kMaxSortPasses) * kRadix * 4));
+  s.tile_ctr = reinterpret_cast<uint32_t*>(take(size_t(kMaxSortPasses) * 4));
+  s.lookback[0] = reinterpret_cast<uint64_t*>(take(size_t(p.tiles) * kRadix * 8));
+  s.lookback[1] = reinterpret_cast<uint64_t*>(take(size_t(p.tiles) * kRadix * 8));
+}
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launches(int n) { g_launches.fetch_add(uint64_t(n), std::memory_order_relaxed); }
+uint64_t launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
+
+CloudTree cloud_tree_facts(int64_t n) { return tree_facts(n); }
+int64_t cloud_tree_blocks(const CloudTree& t) { return tree_blocks_of(t); }
+int64_t cloud_tree_counters(const CloudTree& t) { return tree_counters_of(t); }
+
+unsigned* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tbvh_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<unsigned*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+cudaError_t read_device_status(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_tbvh_status, sizeof(unsigned));
+  if (e != cudaSuccess) return e;
+  if (clear) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_tbvh_status, &zero, sizeof(unsigned));
+  }
+  return e;
+}
+
+static int grid_for(int64_t work, int per_block, int cap) {
+  int64_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return int(g);
+}
+
+// Runs the radix passes over keys already in ss.keys[0] (values implicit).
+static cudaError_t run_sort_passes(const SortPlan& p, const SortScratch& ss, const CloudMap& cm,
+                                   int64_t* final_out, cudaStream_t stream) {
+  const size_t smem = sizeof(PassSmem);
+  static_assert(sizeof(PassSmem) <= 48 * 1024, "pass tile must fit the default dynamic shared memory limit");
+  unsigned* status = device_status_ptr();
+  int src = 0;
+  for (int ps = 0; ps < p.passes; ++ps) {
+    PassArgs a{};
+    a.keys_in = ss.keys[src];
+    a.vals_in = ps == 0 ? nullptr : ss.vals[src];
+    const bool last = ps == p.passes - 1;
+    a.keys_out = last ? nullptr : ss.keys[src ^ 1];
+    a.vals_out = last ? nullptr : ss.vals[src ^ 1];
+    a.final_out = last ? final_out : nullptr;
+    a.hist = ss.hist + ps * kRadix;
+    a.lookback = ss.lookback[ps & 1];
+    a.lookback_next = last ? nullptr : ss.lookback[(ps + 1) & 1];
+    a.tile_ctr = ss.tile_ctr + ps;
+    a.n = p.n;
+    a.lo_bit = 8 * ps;
+    a.code_bits = p.code_bits;
+    a.needs_cloud = (8 * ps + 8 > p.code_bits && p.cloud_bits > 0) || (last && cm.num_clouds > 1) ? 1 : 0;
+    a.cm = cm;
+    a.status = status;
+    k_sort_pass<<<dim3(unsigned(p.tiles)), kSortThreads, smem, stream>>>(a);
+    count_launches(1);
+    src ^= 1;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream) {
+  const int D = b.dim;
+  const SortPlan& p = b.sort;
+  const int64_t n = p.n;
+  // 1. init
+  InitArgs ia{};
+  ia.zero[0] = {b.ss.hist, int64_t(kMaxSortPasses) * kRadix};
+  ia.zero[1] = {b.ss.tile_ctr, int64_t(kMaxSortPasses)};
+  ia.zero[2] = {reinterpret_cast<uint32_t*>(b.ss.lookback[0]), p.tiles * kRadix * 2};
+  ia.zero[3] = {b.tree_counter, b.tree_counters};
+  ia.bounds_enc = b.bounds_enc;
+  ia.bounds_words = b.clouds.num_clouds * 2 * D;
+  ia.dim = D;
+  ia.clouds = b.clouds;
+  ia.table = b.clouds.uniform_n > 0 ? nullptr : b.table;
+  const int64_t init_work = p.tiles * kRadix * 2 > b.tree_counters ? p.tiles * kRadix * 2 : b.tree_counters;
+  k_init<<<grid_for(init_work, 256 * 4, 1184), 256, 0, stream>>>(ia);
+  count_launches(1);
+  // 2. bounds
+  const int64_t chunk = n / 1184 > 4096 ? ((n / 1184 + 255) / 256) * 256 : 4096;
+  const int bgrid = int((n + chunk - 1) / chunk);
+  if (D == 3) k_bounds<3><<<bgrid, 256, 0, stream>>>(b.points, b.clouds, n, chunk, b.bounds_enc);
+  else k_bounds<2><<<bgrid, 256, 0, stream>>>(b.points, b.clouds, n, chunk, b.bounds_enc);
+  count_launches(1);
+  // 3. keys + histograms
+  const int kgrid = grid_for(n, 256, 148 * 8);
+  if (D == 3)
+    k_keys<3, true><<<kgrid, 256, 0, stream>>>(b.points, b.clouds, n, b.bounds_enc, nullptr, nullptr,
+                                                b.ss.keys[0], b.ss.hist, p.code_bits, p.passes,
+                                                b.scene_min, b.scene_max);
+  else
+    k_keys<2, true><<<kgrid, 256, 0, stream>>>(b.points, b.clouds, n, b.bounds_enc, nullptr, nullptr,
+                                                b.ss.keys[0], b.ss.hist, p.code_bits, p.passes,
+                                                b.scene_min, b.scene_max);
+  count_launches(1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // 4. radix passes -> sorted_indices
+  e = run_sort_passes(p, b.ss, b.clouds, b.sorted_indices, stream);
+  if (e != cudaSuccess) return e;
+  // 5. tree
+  TreeArgs ta{};
+  ta.points = b.points;
+  ta.sorted = b.sorted_indices;
+  ta.node_aabbs = b.node_aabbs;
+  ta.left = b.left_child;
+  ta.right = b.right_child;
+  ta.m2l = b.mem_to_leaf;
+  ta.arrays_per_cloud = b.arrays_per_cloud ? 1 : 0;
+  ta.cm = b.clouds;
+  ta.table = b.clouds.uniform_n > 0 ? nullptr : b.table;
+  ta.uni = b.uniform;
+  ta.uni_blocks = b.clouds.uniform_n > 0 ? cloud_tree_blocks(b.uniform) : 0;
+  ta.uni_rows = b.uniform_rows;
+  ta.uni_counters = b.clouds.uniform_n > 0 ? cloud_tree_counters(b.uniform) : 0;
+  ta.counters = b.tree_counter;
+  ta.status = device_status_ptr();
+  if (D == 3) k_tree<3><<<unsigned(b.tree_blocks), kTreeThreads, 0, stream>>>(ta);
+  else k_tree<2><<<unsigned(b.tree_blocks), kTreeThreads, 0, stream>>>(ta);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream) {
+  const int D = q.dim;
+  const SortPlan& p = q.sort;
+  const int64_t n = p.n;
+  InitArgs ia{};
+  ia.zero[0] = {q.ss.hist, int64_t(kMaxSortPasses) * kRadix};
+  ia.zero[1] = {q.ss.tile_ctr, int64_t(kMaxSortPasses)};
+  ia.zero[2] = {reinterpret_cast<uint32_t*>(q.ss.lookback[0]), p.tiles * kRadix * 2};
+  ia.dim = D;
+  ia.clouds = q.clouds;
+  k_init<<<grid_for(p.tiles * kRadix * 2, 256 * 4, 1184), 256, 0, stream>>>(ia);
+  count_launches(1);
+  const int kgrid = grid_for(n, 256, 148 * 8);
+  if (D == 3)
+    k_keys<3, false><<<kgrid, 256, 0, stream>>>(q.queries, q.clouds, n, nullptr, q.scene_min, q.scene_max,
+                                                 q.ss.keys[0], q.ss.hist, p.code_bits, p.passes, nullptr, nullptr);
+  else
+    k_keys<2, false><<<kgrid, 256, 0, stream>>>(q.queries, q.clouds, n, nullptr, q.scene_min, q.scene_max,
+                                                 q.ss.keys[0], q.ss.hist, p.code_bits, p.passes, nullptr, nullptr);
+  count_launches(1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return run_sort_passes(p, q.ss, q.clouds, q.order_out, stream);
+}
+
+}  // namespace tbvh

@@ -1,0 +1,125 @@
+// Host-visible launch interface between the C-ABI layer (tbvh_capi.cu) and the
+// kernel translation units (tbvh_build.cu, tbvh_knn.cu). No torch types.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "tbvh_common.cuh"
+
+namespace tbvh {
+
+// ---- radix sort (stable LSD, 8-bit digits, decoupled look-back) -----------
+constexpr int kSortThreads = 256;
+constexpr int kSortIpt = 16;
+constexpr int kSortTile = kSortThreads * kSortIpt;  // elements per tile
+constexpr int kRadix = 256;
+constexpr int kMaxSortPasses = 8;
+
+// The sort key of element e is the composite (cloud(e) << code_bits) | code(e);
+// pass p orders by composite bits [8p, 8p + 8). Values are packed element
+// indices, so the cloud of an element is recovered from its value.
+struct SortPlan {
+  int code_bits = 0;   // 30 (3-D) or 32 (2-D)
+  int cloud_bits = 0;  // ceil(log2(num_clouds))
+  int passes = 0;
+  int64_t n = 0;       // elements
+  int64_t tiles = 0;
+};
+
+SortPlan make_sort_plan(int64_t n, int num_clouds, int dim);
+
+struct SortScratch {
+  uint32_t* keys[2];
+  uint32_t* vals[2];
+  uint32_t* hist;         // passes x 256
+  uint32_t* tile_ctr;     // passes
+  uint64_t* lookback[2];  // 2 x (tiles x 256), ping-pong between passes
+};
+
+size_t sort_scratch_bytes(const SortPlan& plan);
+void carve_sort_scratch(const SortPlan& plan, char*& cursor, SortScratch& s);
+
+// ---- build -----------------------------------------------------------------
+constexpr int kTreeThreads = 256;
+constexpr int kTreeSubLevels = 10;  // one build block owns 2^10 leaves
+constexpr int kTreeHopLevels = 8;   // upper levels are merged 8 levels per hop
+
+// Host-side per-cloud facts (the device table mirrors this for ragged input).
+CloudTree cloud_tree_facts(int64_t n);
+int64_t cloud_tree_blocks(const CloudTree& t);
+int64_t cloud_tree_counters(const CloudTree& t);
+
+struct BuildLaunch {
+  // inputs
+  const float* points;
+  CloudMap clouds;
+  int dim;
+  // outputs
+  float* node_aabbs;
+  int64_t* sorted_indices;
+  float* scene_min;
+  float* scene_max;
+  int32_t* left_child;   // nullable
+  int32_t* right_child;  // nullable
+  int32_t* mem_to_leaf;  // nullable
+  bool arrays_per_cloud;
+  // plan
+  SortPlan sort;
+  int64_t tree_blocks;
+  int64_t tree_counters;
+  CloudTree uniform;        // valid when clouds.uniform_n > 0
+  int64_t uniform_rows;     // nr of one uniform cloud
+  // scratch
+  SortScratch ss;
+  uint32_t* bounds_enc;     // num_clouds x 2D
+  CloudTree* table;         // ragged only
+  uint32_t* tree_counter;   // tree_counters entries
+};
+
+cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream);
+
+struct QuerySortLaunch {
+  const float* queries;
+  CloudMap clouds;
+  int dim;
+  const float* scene_min;
+  const float* scene_max;
+  int64_t* order_out;
+  SortPlan sort;
+  SortScratch ss;
+};
+
+cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream);
+
+// ---- k-NN traversal ----------------------------------------------------------
+struct KnnLaunch {
+  const float* node_aabbs;
+  const int64_t* sorted_indices;
+  const float* queries;
+  const int64_t* order;  // nullable: identity order
+  int64_t* out_idx;
+  float* out_dist;
+  CloudMap points;
+  CloudMap queries_map;
+  const CloudTree* table;  // ragged only (written by launch_knn's init kernel)
+  CloudTree* table_scratch;
+  CloudTree uniform;
+  int64_t uniform_rows;
+  int64_t total_queries;
+  int dim;
+  int k;
+};
+
+cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream);
+
+// Host-side count of kernel launches issued by this library (all devices).
+void count_launches(int n);
+uint64_t launches_so_far();
+
+// Device status word (error bits from bounded waits / guards), per device.
+cudaError_t read_device_status(unsigned* out, bool clear);
+unsigned* device_status_ptr();
+
+}  // namespace tbvh

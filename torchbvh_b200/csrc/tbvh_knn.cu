@@ -1,0 +1,357 @@
+// Exact k-NN traversal for the B200 path.
+//
+// Replaces query_knn_batched_cached_bounds_kernel and its launchers
+// (torchbvh/csrc/knn_query.cu:20-181,329-446). Same inputs (node_aabbs in the
+// reference's memory order, int64 sorted_indices, optional Morton query
+// order), same outputs (int64 local indices and float32 squared distances,
+// ascending, written at the query's original row).
+//
+// Design (B200-first rather than one independent thread per query):
+//  * One warp serves 32 consecutive queries of the (Morton-)sorted order, so
+//    its queries are spatial neighbours. The warp walks the implicit tree as a
+//    packet: a node is entered when any lane's lower bound admits it, child
+//    order is a lane majority vote, and the deferred-sibling stack keeps the
+//    node id once per warp plus one bound per lane in shared memory. Node box
+//    loads are warp-uniform (one transaction each).
+//  * The tree is cut 5 levels above the leaves: a node there covers <= 32
+//    consecutive sorted leaves ("bucket"), which the warp stages into shared
+//    memory with one coalesced load (coordinates + original index) and then
+//    scans with broadcast reads, every lane testing every point.
+//  * Each lane keeps its top-k sorted in registers, ordered by (distance,
+//    original index). Pruning keeps the reference's rule (skip a node only if
+//    its lower bound is strictly greater than the k-th distance), so the
+//    result is the exact k smallest (distance, index) pairs: identical to the
+//    reference except for the order among exactly tied distances, which the
+//    reference leaves unspecified (docs/algorithms.md, k-NN Query).
+//  * Queries of several clouds may share a warp (ragged batches); the warp
+//    serves each cloud in turn with the other lanes disabled.
+#include "tbvh_kernels.h"
+
+namespace tbvh {
+namespace {
+
+constexpr int kKnnThreads = 256;
+constexpr int kKnnWarps = kKnnThreads / 32;
+constexpr int kBucketLevels = 5;  // bucket = 32 leaves
+constexpr int kStackDepth = 32;
+
+struct KnnArgs {
+  const float* node_aabbs;
+  const int64_t* sorted;
+  const float* queries;
+  const int64_t* order;
+  int64_t* out_idx;
+  float* out_dist;
+  CloudMap pts;
+  CloudMap qry;
+  const CloudTree* table;
+  CloudTree uni;
+  int64_t uni_rows;
+  int64_t total_q;
+  unsigned* status;
+};
+
+struct KnnSmem {
+  float4 bucket[kKnnWarps][32];
+  float stack_dist[kKnnWarps][kStackDepth][32];
+  uint32_t stack_node[kKnnWarps][kStackDepth];
+};
+
+template <int K>
+__device__ __forceinline__ void topk_insert(float (&kd)[K], int32_t (&ki)[K], float d, int32_t idx) {
+  kd[K - 1] = d;
+  ki[K - 1] = idx;
+#pragma unroll
+  for (int s = K - 1; s > 0; --s) {
+    const bool sw = kd[s] < kd[s - 1] || (kd[s] == kd[s - 1] && ki[s] < ki[s - 1]);
+    const float dlo = sw ? kd[s] : kd[s - 1];
+    const float dhi = sw ? kd[s - 1] : kd[s];
+    const int32_t ilo = sw ? ki[s] : ki[s - 1];
+    const int32_t ihi = sw ? ki[s - 1] : ki[s];
+    kd[s - 1] = dlo;
+    kd[s] = dhi;
+    ki[s - 1] = ilo;
+    ki[s] = ihi;
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void load_box(const float* rows, int64_t row, float* lo, float* hi) {
+  const float* r = rows + row * (2 * D);
+  if constexpr (D == 3) {
+    const float2 a = __ldg(reinterpret_cast<const float2*>(r));
+    const float2 b = __ldg(reinterpret_cast<const float2*>(r) + 1);
+    const float2 c = __ldg(reinterpret_cast<const float2*>(r) + 2);
+    lo[0] = a.x; lo[1] = a.y; lo[2] = b.x;
+    hi[0] = b.y; hi[1] = c.x; hi[2] = c.y;
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(r));
+    lo[0] = a.x; lo[1] = a.y;
+    hi[0] = a.z; hi[1] = a.w;
+  }
+}
+
+template <int D, int K>
+__device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int cloud, bool mine, int64_t pos,
+                                             unsigned lane, unsigned warp) {
+  // Cloud facts.
+  CloudTree t;
+  if (a.table) {
+    t = a.table[cloud];
+  } else {
+    t = a.uni;
+    t.row_off = int64_t(cloud) * a.uni_rows;
+  }
+  const int64_t n = t.n;
+  const int L = t.leaf_level;
+  const int Lb = L > kBucketLevels ? L - kBucketLevels : 0;
+  const int bucket_span = L - Lb;
+  const int64_t pt_off = a.pts.start(cloud);
+  const int64_t q_off = a.qry.start(cloud);
+  const float* rows = a.node_aabbs + t.row_off * (2 * D);
+  const int64_t* sorted = a.sorted + pt_off;
+
+  // Lane l holds cnt(l) and rowoff(l) of level l (l <= L <= 31).
+  const int64_t my_cnt = int(lane) <= L ? level_count(n, L, int(lane)) : 0;
+  int64_t incl = my_cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(kFullMask, incl, o);
+    if (lane >= unsigned(o)) incl += y;
+  }
+  const int64_t my_rowoff = incl - my_cnt;
+  const int64_t leaf_row0 = __shfl_sync(kFullMask, my_rowoff, L);
+
+  // Query.
+  float q[D];
+  int64_t gq = 0;
+#pragma unroll
+  for (int c = 0; c < D; ++c) q[c] = 0.0f;
+  if (mine) {
+    int64_t local = a.order ? a.order[pos] : pos - q_off;
+    if (local < 0 || local >= a.qry.size(cloud)) {  // a foreign or corrupted order; keep the read in bounds
+      atomicOr(a.status, kDevErrBadIndex);
+      local = 0;
+    }
+    gq = q_off + local;
+#pragma unroll
+    for (int c = 0; c < D; ++c) q[c] = a.queries[gq * D + c];
+  }
+
+  float kd[K];
+  int32_t ki[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) { kd[i] = kFar; ki[i] = -1; }
+  float kth = mine ? kFar : -1.0f;  // disabled lanes admit nothing
+
+  int level = 0;
+  int64_t node = 0;
+  float nd;
+  {
+    float lo[D], hi[D];
+    load_box<D>(rows, 0, lo, hi);
+    nd = box_dist2<D>(q, lo, hi);
+  }
+  int sp = 0;
+  if (__any_sync(kFullMask, nd <= kth)) {
+    for (;;) {
+      if (level == Lb) {
+        // Bucket: sorted leaves [node << span, +32) clipped to n.
+        const int64_t start = node << bucket_span;
+        const int64_t rem = n - start;
+        const int count = int(rem < (int64_t(1) << bucket_span) ? rem : (int64_t(1) << bucket_span));
+        if (int(lane) < count) {
+          const float* r = rows + (leaf_row0 + start + lane) * (2 * D);
+          const int32_t src = int32_t(sorted[start + lane]);
+          float4 v;
+          v.x = r[0];
+          v.y = r[1];
+          v.z = D == 3 ? r[2] : 0.0f;
+          v.w = __int_as_float(src);
+          s.bucket[warp][lane] = v;
+        }
+        __syncwarp();
+        for (int i = 0; i < count; ++i) {
+          const float4 p = s.bucket[warp][i];
+          const float d = point_dist2<D>(q, p.x, p.y, p.z);
+          const int32_t idx = __float_as_int(p.w);
+          if (d < kth || (d == kth && idx < ki[K - 1])) {
+            topk_insert<K>(kd, ki, d, idx);
+            kth = kd[K - 1];
+          }
+        }
+        __syncwarp();
+      } else {
+        const int cl = level + 1;
+        const int64_t c0 = node * 2;
+        const int64_t ccnt = __shfl_sync(kFullMask, my_cnt, cl);
+        const int64_t crow = __shfl_sync(kFullMask, my_rowoff, cl) + c0;
+        const bool right_real = c0 + 1 < ccnt;
+        float lo[D], hi[D];
+        load_box<D>(rows, crow, lo, hi);
+        const float d0 = box_dist2<D>(q, lo, hi);
+        float d1 = INFINITY;
+        if (right_real) {
+          load_box<D>(rows, crow + 1, lo, hi);
+          d1 = box_dist2<D>(q, lo, hi);
+        }
+        const bool n0 = d0 <= kth;
+        const bool n1 = d1 <= kth;
+        const bool want = n0 || n1;
+        const bool pref_left = n0 && (!n1 || d0 <= d1);
+        const int votes_left = __popc(__ballot_sync(kFullMask, want && pref_left));
+        const int votes_all = __popc(__ballot_sync(kFullMask, want));
+        const bool left_first = 2 * votes_left >= votes_all;
+        const float near_d = left_first ? d0 : d1;
+        const float far_d = left_first ? d1 : d0;
+        const int64_t near_j = left_first ? c0 : c0 + 1;
+        const int64_t far_j = left_first ? c0 + 1 : c0;
+        if (__any_sync(kFullMask, far_d <= kth)) {
+          if (sp < kStackDepth) {
+            s.stack_dist[warp][sp][lane] = far_d;
+            if (lane == 0) s.stack_node[warp][sp] = uint32_t(far_j) | (uint32_t(cl) << 27);
+            ++sp;
+          } else if (lane == 0) {
+            atomicOr(a.status, kDevErrStackOverflow);
+          }
+        }
+        if (__any_sync(kFullMask, near_d <= kth)) {
+          level = cl;
+          node = near_j;
+          nd = near_d;
+          continue;
+        }
+      }
+      // Pop the next deferred node that some lane still needs.
+      bool found = false;
+      while (sp > 0) {
+        --sp;
+        __syncwarp();
+        const uint32_t e = s.stack_node[warp][sp];
+        const float d = s.stack_dist[warp][sp][lane];
+        if (__any_sync(kFullMask, d <= kth)) {
+          level = int(e >> 27);
+          node = int64_t(e & 0x07ffffffu);
+          nd = d;
+          found = true;
+          break;
+        }
+      }
+      if (!found) break;
+    }
+  }
+  (void)nd;
+
+  if (mine) {
+    int64_t* oi = a.out_idx + gq * K;
+    float* od = a.out_dist + gq * K;
+#pragma unroll
+    for (int i = 0; i < K; i += 2) {
+      reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(ki[i], ki[i + 1]);
+    }
+#pragma unroll
+    for (int i = 0; i < K; i += 4) {
+      reinterpret_cast<float4*>(od)[i / 4] = make_float4(kd[i], kd[i + 1], kd[i + 2], kd[i + 3]);
+    }
+  }
+}
+
+template <int D, int K>
+__global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
+  __shared__ KnnSmem s;
+  const unsigned lane = threadIdx.x & 31u;
+  const unsigned warp = threadIdx.x >> 5;
+  const int64_t pos = (int64_t(blockIdx.x) * kKnnWarps + warp) * 32 + lane;
+  const bool valid = pos < a.total_q;
+  const int cloud = valid ? a.qry.find(pos) : -1;
+  unsigned pending = __ballot_sync(kFullMask, valid);
+  while (pending) {
+    const int leader = __ffs(pending) - 1;
+    const int cur = __shfl_sync(kFullMask, cloud, leader);
+    const bool mine = valid && cloud == cur;
+    pending &= ~__ballot_sync(kFullMask, mine);
+    search_cloud<D, K>(a, s, cur, mine, pos, lane, warp);
+  }
+}
+
+// Per-cloud table for ragged queries (n, leaf level, first node row).
+__global__ void __launch_bounds__(256) k_knn_table(CloudMap pts, CloudTree* table) {
+  __shared__ int64_t s_warp[8];
+  int64_t carry = 0;
+  for (int base = 0; base < pts.num_clouds; base += 256) {
+    const int b = base + int(threadIdx.x);
+    const bool valid = b < pts.num_clouds;
+    const int64_t n = valid ? pts.size(b) : 0;
+    const int64_t rows = n > 0 ? real_node_count(n) : 0;
+    // Inclusive warp scan + block combine (same pattern as the build init).
+    const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    int64_t x = rows;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(kFullMask, x, o);
+      if (lane >= unsigned(o)) x += y;
+    }
+    if (lane == 31) s_warp[warp] = x;
+    __syncthreads();
+    int64_t before = 0, total = 0;
+    for (int w = 0; w < 8; ++w) {
+      if (w < int(warp)) before += s_warp[w];
+      total += s_warp[w];
+    }
+    if (valid) {
+      CloudTree t{};
+      t.n = n;
+      t.leaf_level = ceil_log2_i64(n);
+      t.row_off = carry + before + x - rows;
+      table[b] = t;
+    }
+    carry += total;
+    __syncthreads();
+  }
+}
+
+template <int D, int K>
+cudaError_t launch_typed(const KnnArgs& a, cudaStream_t stream) {
+  const int64_t warps = (a.total_q + 31) / 32;
+  const int64_t blocks = (warps + kKnnWarps - 1) / kKnnWarps;
+  if (blocks > 0) {
+    k_knn<D, K><<<unsigned(blocks), kKnnThreads, 0, stream>>>(a);
+    count_launches(1);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream) {
+  KnnArgs a{};
+  a.node_aabbs = q.node_aabbs;
+  a.sorted = q.sorted_indices;
+  a.queries = q.queries;
+  a.order = q.order;
+  a.out_idx = q.out_idx;
+  a.out_dist = q.out_dist;
+  a.pts = q.points;
+  a.qry = q.queries_map;
+  a.uni = q.uniform;
+  a.uni_rows = q.uniform_rows;
+  a.total_q = q.total_queries;
+  a.status = device_status_ptr();
+  if (q.points.uniform_n > 0) {
+    a.table = nullptr;
+  } else {
+    k_knn_table<<<1, 256, 0, stream>>>(q.points, q.table_scratch);
+    count_launches(1);
+    a.table = q.table_scratch;
+  }
+  const int D = q.dim;
+  switch (q.k) {
+    case 4: return D == 3 ? launch_typed<3, 4>(a, stream) : launch_typed<2, 4>(a, stream);
+    case 8: return D == 3 ? launch_typed<3, 8>(a, stream) : launch_typed<2, 8>(a, stream);
+    case 16: return D == 3 ? launch_typed<3, 16>(a, stream) : launch_typed<2, 16>(a, stream);
+    case 32: return D == 3 ? launch_typed<3, 32>(a, stream) : launch_typed<2, 32>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tbvh
