@@ -1,0 +1,169 @@
+"""Multi-GPU k-NN over ``torch.distributed`` (one process per GPU).
+
+The reference is single-GPU; this module adds the sharded forms of its three
+input shapes:
+
+* ``knn_sharded_single_cloud``: one large cloud. Rank ``src`` holds the
+  points; they are broadcast (NCCL over NVLink), every rank builds the same
+  BVH, takes a contiguous slice of the queries, queries it, and the result
+  slices are all-gathered (or gathered to ``src``).
+* ``knn_sharded_batched``: fixed-size batches, clouds split contiguously over
+  ranks, results all-gathered in cloud order.
+* ``knn_sharded_ragged``: ragged batches, clouds assigned by a size-balanced
+  greedy partition (largest first onto the least-loaded rank), results
+  returned in the original packed order.
+
+The collectives are the only data exchange. ``knn_fn`` defaults to this
+package's CUDA path; tests pass a CPU function to exercise the host logic over
+the gloo backend. All ranks call every collective in the same order.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+import torch.distributed as dist
+
+KnnFn = Callable[..., tuple[torch.Tensor, torch.Tensor]]
+
+
+def default_knn(points: torch.Tensor, queries: torch.Tensor, k: int, *, batch_offsets=None,
+                query_offsets=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """One build + query through the public API (the CUDA path)."""
+    from ._bvh_class import BVH
+
+    with BVH(points, batch_offsets=batch_offsets) as bvh:
+        if batch_offsets is not None:
+            return bvh.knn(queries, k, query_offsets=query_offsets)
+        return bvh.knn(queries, k)
+
+
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, end) slice of `total` items owned by `rank` (sizes differ by at most one)."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def partition_clouds(sizes: list[int], world: int) -> list[list[int]]:
+    """Greedy longest-processing-time partition: clouds by size (desc, then index), each
+    onto the currently least-loaded rank (lowest rank on ties). Returns cloud ids per
+    rank, each list in ascending cloud order."""
+    load = [0] * world
+    parts: list[list[int]] = [[] for _ in range(world)]
+    for c in sorted(range(len(sizes)), key=lambda i: (-sizes[i], i)):
+        r = min(range(world), key=lambda j: (load[j], j))
+        parts[r].append(c)
+        load[r] += sizes[c]
+    return [sorted(p) for p in parts]
+
+
+def _world(group) -> tuple[int, int]:
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Tensor:
+    """All-gathers row blocks of different lengths (padded to the longest) and concatenates them."""
+    world, _ = _world(group)
+    width = tuple(local.shape[1:])
+    longest = max(counts)
+    padded = torch.zeros((longest, *width), dtype=local.dtype, device=local.device)
+    padded[: local.shape[0]] = local
+    bufs = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(bufs, padded, group=group)
+    return torch.cat([b[:c] for b, c in zip(bufs, counts)])
+
+
+def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor, k: int, *,
+                             num_points: int, dim: int, src: int = 0, group=None, gather: str = "all",
+                             knn_fn: KnnFn = default_knn, device: torch.device | None = None):
+    """Exact k-NN of one cloud with the queries split over ranks.
+
+    `points` is read on rank `src` only (other ranks may pass None); every rank
+    passes the full `queries` tensor (or a tensor with at least its own slice).
+    `gather`: "all" returns the full (M, k) results on every rank, "root" only
+    on `src` (None elsewhere), "none" returns this rank's slice and its range.
+    """
+    world, rank = _world(group)
+    dev = device or queries.device
+    buf = points if rank == src else torch.empty((num_points, dim), dtype=torch.float32, device=dev)
+    buf = buf.contiguous()
+    dist.broadcast(buf, src=src, group=group)
+    m = queries.shape[0]
+    q0, q1 = shard_range(m, world, rank)
+    idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
+    if gather == "none":
+        return idx, dist_sq, (q0, q1)
+    counts = [shard_range(m, world, r)[1] - shard_range(m, world, r)[0] for r in range(world)]
+    if gather == "root":
+        idx_all = _gather_to(idx, counts, src, group)
+        dist_all = _gather_to(dist_sq, counts, src, group)
+        return (idx_all, dist_all) if rank == src else (None, None)
+    return _all_gather_rows(idx, counts, group), _all_gather_rows(dist_sq, counts, group)
+
+
+def _gather_to(local: torch.Tensor, counts: list[int], dst: int, group) -> torch.Tensor | None:
+    world, rank = _world(group)
+    longest = max(counts)
+    padded = torch.zeros((longest, *local.shape[1:]), dtype=local.dtype, device=local.device)
+    padded[: local.shape[0]] = local
+    bufs = [torch.empty_like(padded) for _ in range(world)] if rank == dst else None
+    dist.gather(padded, bufs, dst=dst, group=group)
+    if rank != dst:
+        return None
+    return torch.cat([b[:c] for b, c in zip(bufs, counts)])
+
+
+def knn_sharded_batched(points: torch.Tensor, queries: torch.Tensor, k: int, *, group=None,
+                        knn_fn: KnnFn = default_knn) -> tuple[torch.Tensor, torch.Tensor]:
+    """(B, N, D) clouds split contiguously over ranks; returns full (B, M, k) on every rank."""
+    world, rank = _world(group)
+    b = points.shape[0]
+    c0, c1 = shard_range(b, world, rank)
+    m = queries.shape[1]
+    if c1 > c0:
+        idx, dist_sq = knn_fn(points[c0:c1].contiguous(), queries[c0:c1].contiguous(), k)
+    else:
+        idx = torch.empty((0, m, k), dtype=torch.int64, device=queries.device)
+        dist_sq = torch.empty((0, m, k), dtype=torch.float32, device=queries.device)
+    counts = [shard_range(b, world, r)[1] - shard_range(b, world, r)[0] for r in range(world)]
+    return _all_gather_rows(idx, counts, group), _all_gather_rows(dist_sq, counts, group)
+
+
+def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: torch.Tensor,
+                       query_offsets: list[int], k: int, *, group=None,
+                       knn_fn: KnnFn = default_knn) -> tuple[torch.Tensor, torch.Tensor]:
+    """Ragged clouds (host offsets) partitioned by size; returns packed (total_M, k) on every rank."""
+    world, rank = _world(group)
+    nb = len(batch_offsets) - 1
+    sizes = [batch_offsets[c + 1] - batch_offsets[c] for c in range(nb)]
+    parts = partition_clouds(sizes, world)
+    mine = parts[rank]
+    dev = queries.device
+    if mine:
+        p_local = torch.cat([points[batch_offsets[c]:batch_offsets[c + 1]] for c in mine])
+        q_local = torch.cat([queries[query_offsets[c]:query_offsets[c + 1]] for c in mine])
+        lo = [0]
+        qlo = [0]
+        for c in mine:
+            lo.append(lo[-1] + sizes[c])
+            qlo.append(qlo[-1] + query_offsets[c + 1] - query_offsets[c])
+        idx, dist_sq = knn_fn(p_local, q_local, k,
+                              batch_offsets=torch.tensor(lo, dtype=torch.int64, device=dev),
+                              query_offsets=torch.tensor(qlo, dtype=torch.int64, device=dev))
+    else:
+        idx = torch.empty((0, k), dtype=torch.int64, device=dev)
+        dist_sq = torch.empty((0, k), dtype=torch.float32, device=dev)
+    qcount = [sum(query_offsets[c + 1] - query_offsets[c] for c in parts[r]) for r in range(world)]
+    all_idx = _all_gather_rows(idx, qcount, group)
+    all_dist = _all_gather_rows(dist_sq, qcount, group)
+    # Back to the original packed order.
+    order = []
+    for r in range(world):
+        for c in parts[r]:
+            order.extend(range(query_offsets[c], query_offsets[c + 1]))
+    inverse = torch.empty(len(order), dtype=torch.int64)
+    inverse[torch.tensor(order, dtype=torch.int64)] = torch.arange(len(order), dtype=torch.int64)
+    inverse = inverse.to(all_idx.device)
+    return all_idx.index_select(0, inverse), all_dist.index_select(0, inverse)
