@@ -91,6 +91,46 @@ __device__ __forceinline__ void load_box(const float* rows, int64_t row, float* 
   }
 }
 
+// Lexicographic (distance, index) order of two top-k slots.
+__device__ __forceinline__ bool slot_less(float da, int32_t ia, float db, int32_t ib) {
+  return da < db || (da == db && ia < ib);
+}
+
+// In-register bitonic sort of the K slots, ascending by (distance, index).
+template <int K>
+__device__ __forceinline__ void topk_sort(float (&kd)[K], int32_t (&ki)[K]) {
+#pragma unroll
+  for (int size = 2; size <= K; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool ascending = (i & size) == 0;
+          const bool out_of_order = ascending ? slot_less(kd[j], ki[j], kd[i], ki[i])
+                                              : slot_less(kd[i], ki[i], kd[j], ki[j]);
+          const float di = kd[i], dj = kd[j];
+          const int32_t ii = ki[i], ij = ki[j];
+          kd[i] = out_of_order ? dj : di;
+          kd[j] = out_of_order ? di : dj;
+          ki[i] = out_of_order ? ij : ii;
+          ki[j] = out_of_order ? ii : ij;
+        }
+      }
+    }
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void load_leaf(const float* rows, int64_t row, float* p) {
+  const float* r = rows + row * (2 * D);
+  const float2 xy = __ldg(reinterpret_cast<const float2*>(r));
+  p[0] = xy.x;
+  p[1] = xy.y;
+  if constexpr (D == 3) p[2] = __ldg(r + 2);
+}
+
 template <int D, int K>
 __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int cloud, bool mine, int64_t pos,
                                              unsigned lane, unsigned warp) {
@@ -122,6 +162,10 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   const int64_t my_rowoff = incl - my_cnt;
   const int64_t leaf_row0 = __shfl_sync(kFullMask, my_rowoff, L);
 
+  // The root box is the scene AABB the Morton codes were taken against.
+  float root_lo[D], root_hi[D];
+  load_box<D>(rows, 0, root_lo, root_hi);
+
   // Query.
   float q[D];
   int64_t gq = 0;
@@ -142,16 +186,61 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   int32_t ki[K];
 #pragma unroll
   for (int i = 0; i < K; ++i) { kd[i] = kFar; ki[i] = -1; }
-  float kth = mine ? kFar : -1.0f;  // disabled lanes admit nothing
 
+  // ---- Seeding. Each lane locates its query's Morton rank among the sorted
+  // leaves (binary search, leaf codes recomputed against the root box) and
+  // scores the `win` leaves around it. Near neighbours sit close to the query
+  // in Morton order, so this makes the k-th distance tight before the exact
+  // traversal starts; that traversal then skips the seeded window per lane.
+  // The window only affects speed: every seeded point is fully evaluated.
+  const int64_t win = n < int64_t(2 * K) ? n : int64_t(2 * K);
+  int64_t w0 = 0;
+  if (mine) {
+    const uint32_t qcode = morton_code<D>(q, root_lo, root_hi);
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      float p[D];
+      load_leaf<D>(rows, leaf_row0 + mid, p);
+      if (morton_code<D>(p, root_lo, root_hi) < qcode) lo = mid + 1; else hi = mid;
+    }
+    w0 = lo - K;
+    if (w0 > n - win) w0 = n - win;
+    if (w0 < 0) w0 = 0;
+  }
+  const int64_t w1 = mine ? w0 + win : 0;
+  // First K window points fill the list unconditionally, then one bitonic sort.
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    if (mine) {
+      float p[D];
+      load_leaf<D>(rows, leaf_row0 + w0 + i, p);
+      const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
+      // Same acceptance as an insertion into an empty list: only d < FLT_MAX enters.
+      const bool ok = d < kFar;
+      kd[i] = ok ? d : kFar;
+      ki[i] = ok ? int32_t(sorted[w0 + i]) : -1;
+    }
+  }
+  topk_sort<K>(kd, ki);
+  float kth = mine ? kd[K - 1] : -1.0f;  // disabled lanes admit nothing
+  for (int64_t i = K; i < win; ++i) {
+    if (mine) {
+      float p[D];
+      load_leaf<D>(rows, leaf_row0 + w0 + i, p);
+      const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
+      const int32_t idx = int32_t(sorted[w0 + i]);
+      if (slot_less(d, idx, kth, ki[K - 1])) {
+        topk_insert<K>(kd, ki, d, idx);
+        kth = kd[K - 1];
+      }
+    }
+  }
+
+  // ---- Exact packet traversal from the root.
   int level = 0;
   int64_t node = 0;
-  float nd;
-  {
-    float lo[D], hi[D];
-    load_box<D>(rows, 0, lo, hi);
-    nd = box_dist2<D>(q, lo, hi);
-  }
+  float nd = box_dist2<D>(q, root_lo, root_hi);
   int sp = 0;
   if (__any_sync(kFullMask, nd <= kth)) {
     for (;;) {
@@ -161,23 +250,49 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
         const int64_t rem = n - start;
         const int count = int(rem < (int64_t(1) << bucket_span) ? rem : (int64_t(1) << bucket_span));
         if (int(lane) < count) {
-          const float* r = rows + (leaf_row0 + start + lane) * (2 * D);
+          float p[D];
+          load_leaf<D>(rows, leaf_row0 + start + lane, p);
           const int32_t src = int32_t(sorted[start + lane]);
-          float4 v;
-          v.x = r[0];
-          v.y = r[1];
-          v.z = D == 3 ? r[2] : 0.0f;
-          v.w = __int_as_float(src);
-          s.bucket[warp][lane] = v;
+          s.bucket[warp][lane] = make_float4(p[0], p[1], D == 3 ? p[2] : 0.0f, __int_as_float(src));
         }
         __syncwarp();
-        for (int i = 0; i < count; ++i) {
-          const float4 p = s.bucket[warp][i];
-          const float d = point_dist2<D>(q, p.x, p.y, p.z);
-          const int32_t idx = __float_as_int(p.w);
-          if (d < kth || (d == kth && idx < ki[K - 1])) {
-            topk_insert<K>(kd, ki, d, idx);
-            kth = kd[K - 1];
+        // Pass 1: every lane marks the points within its current k-th distance
+        // (a superset of what it inserts: the exact test is redone in pass 2).
+        uint32_t cand = 0;
+        if (count == 32) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float4 p = s.bucket[warp][i];
+            if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
+          }
+        } else {
+          for (int i = 0; i < count; ++i) {
+            const float4 p = s.bucket[warp][i];
+            if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
+          }
+        }
+        // Points of this lane's seeded window were scored already.
+        const int64_t slo = w0 - start;
+        const int64_t shi = w1 - start;
+        if (shi > 0 && slo < count) {
+          const int b0 = slo > 0 ? int(slo) : 0;
+          const int b1 = shi < count ? int(shi) : count;
+          const uint32_t upto = b1 >= 32 ? 0xffffffffu : ((1u << b1) - 1u);
+          cand &= ~(upto & ~((1u << b0) - 1u));
+        }
+        // Pass 2: insert the marked points one per lane per round, so the warp
+        // pays max-over-lanes(marks) insertions.
+        while (__any_sync(kFullMask, cand != 0u)) {
+          if (cand) {
+            const int i = __ffs(cand) - 1;
+            cand &= cand - 1u;
+            const float4 p = s.bucket[warp][i];
+            const float d = point_dist2<D>(q, p.x, p.y, p.z);
+            const int32_t idx = __float_as_int(p.w);
+            if (slot_less(d, idx, kth, ki[K - 1])) {
+              topk_insert<K>(kd, ki, d, idx);
+              kth = kd[K - 1];
+            }
           }
         }
         __syncwarp();
