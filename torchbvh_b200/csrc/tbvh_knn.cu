@@ -25,6 +25,8 @@
 //    reference leaves unspecified (docs/algorithms.md, k-NN Query).
 //  * Queries of several clouds may share a warp (ragged batches); the warp
 //    serves each cloud in turn with the other lanes disabled.
+#include <atomic>
+
 #include "tbvh_kernels.h"
 
 namespace tbvh {
@@ -34,6 +36,7 @@ constexpr int kKnnThreads = 256;
 constexpr int kKnnWarps = kKnnThreads / 32;
 constexpr int kBucketLevels = 5;  // bucket = 32 leaves
 constexpr int kStackDepth = 32;
+constexpr int kCandCap = 32;      // deferred candidates per lane
 
 struct KnnArgs {
   const float* node_aabbs;
@@ -51,28 +54,37 @@ struct KnnArgs {
   unsigned* status;
 };
 
+using u64 = unsigned long long;
+
 struct KnnSmem {
   float4 bucket[kKnnWarps][32];
   float stack_dist[kKnnWarps][kStackDepth][32];
   uint32_t stack_node[kKnnWarps][kStackDepth];
+  u64 cand[kKnnWarps][kCandCap][32];  // [slot][lane]: each lane owns one column
 };
 
+// A top-k slot is one 64-bit key: distance bits above, source index below.
+// Squared distances are >= +0, so unsigned key order is (distance, index)
+// order. The empty slot (FLT_MAX, -1) is the largest key any accepted
+// candidate can be compared with: candidates need distance < FLT_MAX, as for
+// the reference's insertion into an empty list.
+__device__ __forceinline__ u64 pack_key(float d, int32_t idx) {
+  return (u64(__float_as_uint(d)) << 32) | u64(uint32_t(idx));
+}
+__device__ __forceinline__ float key_dist(u64 k) { return __uint_as_float(uint32_t(k >> 32)); }
+__device__ __forceinline__ int32_t key_idx(u64 k) { return int32_t(uint32_t(k)); }
+constexpr u64 kEmptyKey = (u64(0x7f7fffffu) << 32) | u64(0xffffffffu);
+
+// Inserts nk (nk < key[K-1]) into the ascending list. Every slot decides its
+// new value from two independent comparisons, so there is no serial chain.
 template <int K>
-__device__ __forceinline__ void topk_insert(float (&kd)[K], int32_t (&ki)[K], float d, int32_t idx) {
-  kd[K - 1] = d;
-  ki[K - 1] = idx;
+__device__ __forceinline__ void topk_insert(u64 (&key)[K], u64 nk) {
+  bool before[K];
 #pragma unroll
-  for (int s = K - 1; s > 0; --s) {
-    const bool sw = kd[s] < kd[s - 1] || (kd[s] == kd[s - 1] && ki[s] < ki[s - 1]);
-    const float dlo = sw ? kd[s] : kd[s - 1];
-    const float dhi = sw ? kd[s - 1] : kd[s];
-    const int32_t ilo = sw ? ki[s] : ki[s - 1];
-    const int32_t ihi = sw ? ki[s - 1] : ki[s];
-    kd[s - 1] = dlo;
-    kd[s] = dhi;
-    ki[s - 1] = ilo;
-    ki[s] = ihi;
-  }
+  for (int s = 0; s < K; ++s) before[s] = nk < key[s];
+#pragma unroll
+  for (int s = K - 1; s > 0; --s) key[s] = before[s] ? (before[s - 1] ? key[s - 1] : nk) : key[s];
+  key[0] = before[0] ? nk : key[0];
 }
 
 template <int D>
@@ -91,14 +103,9 @@ __device__ __forceinline__ void load_box(const float* rows, int64_t row, float* 
   }
 }
 
-// Lexicographic (distance, index) order of two top-k slots.
-__device__ __forceinline__ bool slot_less(float da, int32_t ia, float db, int32_t ib) {
-  return da < db || (da == db && ia < ib);
-}
-
-// In-register bitonic sort of the K slots, ascending by (distance, index).
+// In-register bitonic sort of the K keys, ascending.
 template <int K>
-__device__ __forceinline__ void topk_sort(float (&kd)[K], int32_t (&ki)[K]) {
+__device__ __forceinline__ void topk_sort(u64 (&key)[K]) {
 #pragma unroll
   for (int size = 2; size <= K; size <<= 1) {
 #pragma unroll
@@ -108,14 +115,10 @@ __device__ __forceinline__ void topk_sort(float (&kd)[K], int32_t (&ki)[K]) {
         const int j = i ^ stride;
         if (j > i) {
           const bool ascending = (i & size) == 0;
-          const bool out_of_order = ascending ? slot_less(kd[j], ki[j], kd[i], ki[i])
-                                              : slot_less(kd[i], ki[i], kd[j], ki[j]);
-          const float di = kd[i], dj = kd[j];
-          const int32_t ii = ki[i], ij = ki[j];
-          kd[i] = out_of_order ? dj : di;
-          kd[j] = out_of_order ? di : dj;
-          ki[i] = out_of_order ? ij : ii;
-          ki[j] = out_of_order ? ii : ij;
+          const u64 a = key[i], b = key[j];
+          const bool swap = ascending ? b < a : a < b;
+          key[i] = swap ? b : a;
+          key[j] = swap ? a : b;
         }
       }
     }
@@ -182,10 +185,32 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     for (int c = 0; c < D; ++c) q[c] = a.queries[gq * D + c];
   }
 
-  float kd[K];
-  int32_t ki[K];
+  u64 key[K];
 #pragma unroll
-  for (int i = 0; i < K; ++i) { kd[i] = kFar; ki[i] = -1; }
+  for (int i = 0; i < K; ++i) key[i] = kEmptyKey;
+
+  // Deferred candidates: each lane appends keys that beat its k-th key when
+  // they are found and inserts them in rounds (one per lane per round) when
+  // its buffer would overflow and at the end, so a warp pays about
+  // max-over-lanes(candidates) insertions instead of one round per bucket in
+  // which any lane found something.
+  u64 (*cbuf)[32] = s.cand[warp];
+  int ccount = 0;
+  u64 kth_key = mine ? kEmptyKey : 0ull;  // disabled lanes admit nothing
+  float kth = mine ? kFar : -1.0f;
+  auto flush = [&]() {
+    while (__any_sync(kFullMask, ccount > 0)) {
+      if (ccount > 0) {
+        --ccount;
+        const u64 nk = cbuf[ccount][lane];
+        if (nk < kth_key) {
+          topk_insert<K>(key, nk);
+          kth_key = key[K - 1];
+          kth = key_dist(kth_key);
+        }
+      }
+    }
+  };
 
   // ---- Seeding. Each lane locates its query's Morton rank among the sorted
   // leaves (binary search, leaf codes recomputed against the root box) and
@@ -209,33 +234,33 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     if (w0 < 0) w0 = 0;
   }
   const int64_t w1 = mine ? w0 + win : 0;
-  // First K window points fill the list unconditionally, then one bitonic sort.
+  // The first K window points fill the list (only distances < FLT_MAX enter,
+  // as with insertions into an empty list), then one bitonic sort.
 #pragma unroll
   for (int i = 0; i < K; ++i) {
     if (mine) {
       float p[D];
       load_leaf<D>(rows, leaf_row0 + w0 + i, p);
       const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      // Same acceptance as an insertion into an empty list: only d < FLT_MAX enters.
-      const bool ok = d < kFar;
-      kd[i] = ok ? d : kFar;
-      ki[i] = ok ? int32_t(sorted[w0 + i]) : -1;
+      key[i] = d < kFar ? pack_key(d, int32_t(sorted[w0 + i])) : kEmptyKey;
     }
   }
-  topk_sort<K>(kd, ki);
-  float kth = mine ? kd[K - 1] : -1.0f;  // disabled lanes admit nothing
+  topk_sort<K>(key);
+  if (mine) {
+    kth_key = key[K - 1];
+    kth = key_dist(kth_key);
+  }
+  // The rest of the window (at most K <= kCandCap points) goes through the buffer.
   for (int64_t i = K; i < win; ++i) {
     if (mine) {
       float p[D];
       load_leaf<D>(rows, leaf_row0 + w0 + i, p);
       const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      const int32_t idx = int32_t(sorted[w0 + i]);
-      if (slot_less(d, idx, kth, ki[K - 1])) {
-        topk_insert<K>(kd, ki, d, idx);
-        kth = kd[K - 1];
-      }
+      const u64 nk = pack_key(d, int32_t(sorted[w0 + i]));
+      if (d < kFar && nk < kth_key) cbuf[ccount++][lane] = nk;
     }
   }
+  flush();
 
   // ---- Exact packet traversal from the root.
   int level = 0;
@@ -256,8 +281,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           s.bucket[warp][lane] = make_float4(p[0], p[1], D == 3 ? p[2] : 0.0f, __int_as_float(src));
         }
         __syncwarp();
-        // Pass 1: every lane marks the points within its current k-th distance
-        // (a superset of what it inserts: the exact test is redone in pass 2).
+        // Pass 1: every lane marks the points within its current k-th distance.
         uint32_t cand = 0;
         if (count == 32) {
 #pragma unroll
@@ -280,19 +304,16 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           const uint32_t upto = b1 >= 32 ? 0xffffffffu : ((1u << b1) - 1u);
           cand &= ~(upto & ~((1u << b0) - 1u));
         }
-        // Pass 2: insert the marked points one per lane per round, so the warp
-        // pays max-over-lanes(marks) insertions.
+        // Pass 2: append the marked points' keys to the lane's buffer.
+        if (__any_sync(kFullMask, ccount + __popc(cand) > kCandCap)) flush();
         while (__any_sync(kFullMask, cand != 0u)) {
           if (cand) {
             const int i = __ffs(cand) - 1;
             cand &= cand - 1u;
             const float4 p = s.bucket[warp][i];
             const float d = point_dist2<D>(q, p.x, p.y, p.z);
-            const int32_t idx = __float_as_int(p.w);
-            if (slot_less(d, idx, kth, ki[K - 1])) {
-              topk_insert<K>(kd, ki, d, idx);
-              kth = kd[K - 1];
-            }
+            const u64 nk = pack_key(d, __float_as_int(p.w));
+            if (d < kFar && nk < kth_key) cbuf[ccount++][lane] = nk;
           }
         }
         __syncwarp();
@@ -337,7 +358,9 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           continue;
         }
       }
-      // Pop the next deferred node that some lane still needs.
+      // Pop the next deferred node that some lane still needs. Bounds are
+      // checked against the k-th distance as of the last flush, which is never
+      // below the true one: pruning stays conservative.
       bool found = false;
       while (sp > 0) {
         --sp;
@@ -355,6 +378,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
       if (!found) break;
     }
   }
+  flush();
   (void)nd;
 
   if (mine) {
@@ -362,18 +386,20 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     float* od = a.out_dist + gq * K;
 #pragma unroll
     for (int i = 0; i < K; i += 2) {
-      reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(ki[i], ki[i + 1]);
+      reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(key[i]), key_idx(key[i + 1]));
     }
 #pragma unroll
     for (int i = 0; i < K; i += 4) {
-      reinterpret_cast<float4*>(od)[i / 4] = make_float4(kd[i], kd[i + 1], kd[i + 2], kd[i + 3]);
+      reinterpret_cast<float4*>(od)[i / 4] =
+          make_float4(key_dist(key[i]), key_dist(key[i + 1]), key_dist(key[i + 2]), key_dist(key[i + 3]));
     }
   }
 }
 
 template <int D, int K>
 __global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
-  __shared__ KnnSmem s;
+  extern __shared__ __align__(16) unsigned char knn_smem_raw[];
+  KnnSmem& s = *reinterpret_cast<KnnSmem*>(knn_smem_raw);
   const unsigned lane = threadIdx.x & 31u;
   const unsigned warp = threadIdx.x >> 5;
   const int64_t pos = (int64_t(blockIdx.x) * kKnnWarps + warp) * 32 + lane;
@@ -430,7 +456,18 @@ cudaError_t launch_typed(const KnnArgs& a, cudaStream_t stream) {
   const int64_t warps = (a.total_q + 31) / 32;
   const int64_t blocks = (warps + kKnnWarps - 1) / kKnnWarps;
   if (blocks > 0) {
-    k_knn<D, K><<<unsigned(blocks), kKnnThreads, 0, stream>>>(a);
+    // Opt in to more than 48 KB of dynamic shared memory, once per device.
+    static std::atomic<uint64_t> opted{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = uint64_t(1) << (dev & 63);
+    if (!(opted.load() & bit)) {
+      const cudaError_t e = cudaFuncSetAttribute(k_knn<D, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(sizeof(KnnSmem)));
+      if (e != cudaSuccess) return e;
+      opted.fetch_or(bit);
+    }
+    k_knn<D, K><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
     count_launches(1);
   }
   return cudaGetLastError();
