@@ -93,6 +93,23 @@ int tbvh_sort_queries(int device, const float* queries, int64_t num_clouds, int6
                       const float* scene_min, const float* scene_max, int64_t* order_out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Query Morton permutation that allocates nothing. No counterpart in the
+ * reference. Same arguments and result as tbvh_sort_queries, minus the
+ * workspace: for callers that cannot allocate device memory, such as a plugin
+ * or FFI binding that only receives the buffers it reads and writes, or a
+ * service that reserves its device memory at start-up and must not call
+ * cudaMalloc later (allocation can stall the device or fail under pressure).
+ * Its scratch is a fixed array inside the library, held in the memory of
+ * every GPU that loads the library until the process exits; one call sorts
+ * at most 262,144 queries (larger calls return TBVH_ERR_BAD_ARG). The first
+ * call on a device looks up that array's device address once, so make it
+ * before any stream capture. Every call reuses the same array: the call
+ * clears what must start at zero, but calls that overlap on the GPU (other
+ * streams, unordered host threads) race on it; keep them on one stream. */
+int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clouds, int64_t queries_per_cloud,
+                              const int64_t* query_offsets_dev, int64_t total_queries, int dim,
+                              const float* scene_min, const float* scene_max, int64_t* order_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Exact k-NN. Replaces query_knn_batched_cached_bounds_cuda and
  * query_knn_batched_cached_bounds_ordered_cuda (torchbvh/csrc/knn_query.cu:

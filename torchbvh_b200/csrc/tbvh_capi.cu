@@ -124,6 +124,11 @@ void plan_build(const Clouds& c, int dim, BuildPlan& p) {
 
 }  // namespace
 
+int tbvh::record_error(int code, const char* message) {
+  g_last_error = message;
+  return code;
+}
+
 extern "C" {
 
 const char* tbvh_last_error(void) { return g_last_error.c_str(); }

@@ -114,6 +114,9 @@ struct KnnLaunch {
 
 cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream);
 
+// Sets the calling thread's tbvh_last_error() text and returns `code`.
+int record_error(int code, const char* message);
+
 // Host-side count of kernel launches issued by this library (all devices).
 void count_launches(int n);
 uint64_t launches_so_far();
