@@ -18,13 +18,16 @@ reference's per-sample Python loop (torchbvh/_query.py:68-85,299-366).
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 import types
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libtorchbvh_b200.so")
+# The in-tree build; TORCHBVH_B200_LIBRARY may name another build of the same sources
+# (e.g. one compiled with different tuning macros).
+LIB_PATH = Path(os.environ.get("TORCHBVH_B200_LIBRARY") or Path(__file__).resolve().with_name("libtorchbvh_b200.so"))
 
 TBVH_OK = 0
 TBVH_ERR_BAD_ARG = 1

@@ -17,26 +17,33 @@
 //    consecutive sorted leaves ("bucket"), which the warp stages into shared
 //    memory with one coalesced load (coordinates + original index) and then
 //    scans with broadcast reads, every lane testing every point.
-//  * Each lane keeps its top-k sorted in registers, ordered by (distance,
-//    original index). Pruning keeps the reference's rule (skip a node only if
+//  * Each lane keeps its top-k sorted in registers as packed (distance bits,
+//    original index) keys, seeded from the sorted leaves around the query's
+//    own Morton rank before the traversal starts. Pruning keeps the reference's rule (skip a node only if
 //    its lower bound is strictly greater than the k-th distance), so the
 //    result is the exact k smallest (distance, index) pairs: identical to the
 //    reference except for the order among exactly tied distances, which the
 //    reference leaves unspecified (docs/algorithms.md, k-NN Query).
 //  * Queries of several clouds may share a warp (ragged batches); the warp
 //    serves each cloud in turn with the other lanes disabled.
-#include <atomic>
-
 #include "tbvh_kernels.h"
 
 namespace tbvh {
 namespace {
 
-constexpr int kKnnThreads = 256;
+// Tuning knobs (compile-time; the defaults are the measured best on B200).
+#ifndef TBVH_KNN_THREADS
+#define TBVH_KNN_THREADS 128
+#endif
+constexpr int kKnnThreads = TBVH_KNN_THREADS;
 constexpr int kKnnWarps = kKnnThreads / 32;
-constexpr int kBucketLevels = 5;  // bucket = 32 leaves
-constexpr int kStackDepth = 32;
-constexpr int kCandCap = 32;      // deferred candidates per lane
+#ifndef TBVH_KNN_BUCKET_LEVELS
+#define TBVH_KNN_BUCKET_LEVELS 5
+#endif
+constexpr int kBucketLevels = TBVH_KNN_BUCKET_LEVELS;  // bucket = 2^levels leaves (<= 32)
+constexpr int kBucketSize = 1 << kBucketLevels;
+static_assert(kBucketSize <= 32, "a bucket is staged by one warp");
+constexpr int kStackDepth = 28;   // >= deepest bucket level + 1 for N < 2^31 (27)
 
 struct KnnArgs {
   const float* node_aabbs;
@@ -60,7 +67,6 @@ struct KnnSmem {
   float4 bucket[kKnnWarps][32];
   float stack_dist[kKnnWarps][kStackDepth][32];
   uint32_t stack_node[kKnnWarps][kStackDepth];
-  u64 cand[kKnnWarps][kCandCap][32];  // [slot][lane]: each lane owns one column
 };
 
 // A top-k slot is one 64-bit key: distance bits above, source index below.
@@ -189,26 +195,14 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
 #pragma unroll
   for (int i = 0; i < K; ++i) key[i] = kEmptyKey;
 
-  // Deferred candidates: each lane appends keys that beat its k-th key when
-  // they are found and inserts them in rounds (one per lane per round) when
-  // its buffer would overflow and at the end, so a warp pays about
-  // max-over-lanes(candidates) insertions instead of one round per bucket in
-  // which any lane found something.
-  u64 (*cbuf)[32] = s.cand[warp];
-  int ccount = 0;
-  u64 kth_key = mine ? kEmptyKey : 0ull;  // disabled lanes admit nothing
-  float kth = mine ? kFar : -1.0f;
-  auto flush = [&]() {
-    while (__any_sync(kFullMask, ccount > 0)) {
-      if (ccount > 0) {
-        --ccount;
-        const u64 nk = cbuf[ccount][lane];
-        if (nk < kth_key) {
-          topk_insert<K>(key, nk);
-          kth_key = key[K - 1];
-          kth = key_dist(kth_key);
-        }
-      }
+  float kth = mine ? kFar : -1.0f;  // disabled lanes admit nothing
+  u64 kth_key = mine ? kEmptyKey : 0ull;
+  // Offers a candidate key whose distance is already known to be < FLT_MAX.
+  auto offer = [&](u64 nk) {
+    if (nk < kth_key) {
+      topk_insert<K>(key, nk);
+      kth_key = key[K - 1];
+      kth = key_dist(kth_key);
     }
   };
 
@@ -250,17 +244,15 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     kth_key = key[K - 1];
     kth = key_dist(kth_key);
   }
-  // The rest of the window (at most K <= kCandCap points) goes through the buffer.
+  // The rest of the window.
   for (int64_t i = K; i < win; ++i) {
     if (mine) {
       float p[D];
       load_leaf<D>(rows, leaf_row0 + w0 + i, p);
       const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      const u64 nk = pack_key(d, int32_t(sorted[w0 + i]));
-      if (d < kFar && nk < kth_key) cbuf[ccount++][lane] = nk;
+      if (d < kFar) offer(pack_key(d, int32_t(sorted[w0 + i])));
     }
   }
-  flush();
 
   // ---- Exact packet traversal from the root.
   int level = 0;
@@ -283,9 +275,9 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
         __syncwarp();
         // Pass 1: every lane marks the points within its current k-th distance.
         uint32_t cand = 0;
-        if (count == 32) {
+        if (count == kBucketSize) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < kBucketSize; ++i) {
             const float4 p = s.bucket[warp][i];
             if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
           }
@@ -304,16 +296,15 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           const uint32_t upto = b1 >= 32 ? 0xffffffffu : ((1u << b1) - 1u);
           cand &= ~(upto & ~((1u << b0) - 1u));
         }
-        // Pass 2: append the marked points' keys to the lane's buffer.
-        if (__any_sync(kFullMask, ccount + __popc(cand) > kCandCap)) flush();
+        // Pass 2: insert the marked points, one per lane per round, so the warp
+        // pays max-over-lanes(marks) insertions per bucket.
         while (__any_sync(kFullMask, cand != 0u)) {
           if (cand) {
             const int i = __ffs(cand) - 1;
             cand &= cand - 1u;
             const float4 p = s.bucket[warp][i];
             const float d = point_dist2<D>(q, p.x, p.y, p.z);
-            const u64 nk = pack_key(d, __float_as_int(p.w));
-            if (d < kFar && nk < kth_key) cbuf[ccount++][lane] = nk;
+            if (d < kFar) offer(pack_key(d, __float_as_int(p.w)));
           }
         }
         __syncwarp();
@@ -358,9 +349,8 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           continue;
         }
       }
-      // Pop the next deferred node that some lane still needs. Bounds are
-      // checked against the k-th distance as of the last flush, which is never
-      // below the true one: pruning stays conservative.
+      // Pop the next deferred node that some lane still needs (against the
+      // lane's current k-th distance).
       bool found = false;
       while (sp > 0) {
         --sp;
@@ -378,7 +368,6 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
       if (!found) break;
     }
   }
-  flush();
   (void)nd;
 
   if (mine) {
@@ -456,17 +445,7 @@ cudaError_t launch_typed(const KnnArgs& a, cudaStream_t stream) {
   const int64_t warps = (a.total_q + 31) / 32;
   const int64_t blocks = (warps + kKnnWarps - 1) / kKnnWarps;
   if (blocks > 0) {
-    // Opt in to more than 48 KB of dynamic shared memory, once per device.
-    static std::atomic<uint64_t> opted{0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint64_t bit = uint64_t(1) << (dev & 63);
-    if (!(opted.load() & bit)) {
-      const cudaError_t e = cudaFuncSetAttribute(k_knn<D, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(sizeof(KnnSmem)));
-      if (e != cudaSuccess) return e;
-      opted.fetch_or(bit);
-    }
+    static_assert(sizeof(KnnSmem) <= 48 * 1024, "fits the default dynamic shared memory limit");
     k_knn<D, K><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
     count_launches(1);
   }
