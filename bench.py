@@ -382,7 +382,7 @@ def run_b200(args, world, rank, local):
     }
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, args)
 
     result = {

@@ -1,0 +1,107 @@
+"""The multi-GPU layer on real GPUs: NCCL process groups of 2 ranks (one per
+GPU) running the sharded k-NN forms with the CUDA path, compared with the
+single-GPU result. Skipped on machines with fewer than 2 GPUs. NVLS is
+switched off and each group has a short timeout."""
+
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+import traceback
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs():
+    g = torch.Generator().manual_seed(21)
+    big_p = torch.rand((200_000, 3), generator=g)
+    big_q = torch.rand((70_001, 3), generator=g)
+    bp = torch.rand((5, 20_000, 2), generator=g)
+    bq = torch.rand((5, 3_001, 2), generator=g)
+    sizes = [5000, 40_000, 1024, 77_777, 3000]
+    qsizes = [100, 2000, 10, 5000, 333]
+    bo = [0]
+    qo = [0]
+    for a, b in zip(sizes, qsizes):
+        bo.append(bo[-1] + a)
+        qo.append(qo[-1] + b)
+    rp = torch.rand((bo[-1], 3), generator=g)
+    rq = torch.rand((qo[-1], 3), generator=g)
+    return big_p, big_q, bp, bq, rp, bo, rq, qo
+
+
+def _worker(rank, world, port, outdir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from torchbvh_b200 import distributed as tdist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        big_p, big_q, bp, bq, rp, bo, rq, qo = _inputs()
+        out = {}
+        i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, big_q.to(dev), 32,
+                                              num_points=big_p.shape[0], dim=3, device=dev)
+        out["single"] = (i.cpu(), d.cpu())
+        i, d = tdist.knn_sharded_batched(bp.to(dev), bq.to(dev), 8)
+        out["batched"] = (i.cpu(), d.cpu())
+        i, d = tdist.knn_sharded_ragged(rp.to(dev), bo, rq.to(dev), qo, 16)
+        out["ragged"] = (i.cpu(), d.cpu())
+        torch.cuda.synchronize(dev)
+        torch.save(out, Path(outdir) / f"rank{rank}.pt")
+        dist.destroy_process_group()
+    except Exception:
+        (Path(outdir) / f"rank{rank}.err").write_text(traceback.format_exc())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.timeout(600)
+def test_sharded_knn_on_two_gpus_matches_one_gpu():
+    import torchbvh_b200 as torchbvh
+
+    outdir = tempfile.mkdtemp()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, outdir)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    hung = [p for p in procs if p.is_alive()]
+    for p in hung:
+        p.kill()
+    assert not hung, "a rank hung"
+    errs = list(Path(outdir).glob("*.err"))
+    assert not errs, errs[0].read_text()
+    big_p, big_q, bp, bq, rp, bo, rq, qo = _inputs()
+    dev = torch.device("cuda", 0)
+    with torchbvh.BVH(big_p.to(dev)) as bvh:
+        si, sd = bvh.knn(big_q.to(dev), 32)
+    with torchbvh.BVH(bp.to(dev)) as bvh:
+        bi, bd = bvh.knn(bq.to(dev), 8)
+    bot = torch.tensor(bo, device=dev)
+    qot = torch.tensor(qo, device=dev)
+    with torchbvh.BVH(rp.to(dev), batch_offsets=bot) as bvh:
+        ri, rd = bvh.knn(rq.to(dev), 16, query_offsets=qot)
+    for r in range(2):
+        got = torch.load(Path(outdir) / f"rank{r}.pt")
+        assert torch.equal(got["single"][0], si.cpu()) and torch.equal(got["single"][1], sd.cpu())
+        assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
+        assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())
