@@ -56,6 +56,8 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--c4-points", type=int, default=16_777_216,
+                    help="points (= queries) of workload c4; smaller values make ncu-sized cases")
     ap.add_argument("--cpu-sample-queries", type=int, default=0,
                     help="queries per sampled cloud for the CPU baseline (0 = automatic)")
     return ap.parse_args()
@@ -184,9 +186,11 @@ class ClockSampler:
 # workload helpers
 # ---------------------------------------------------------------------------
 
-def load_workload(name: str):
+def load_workload(name: str, args=None):
     from torchbvh_b200 import workloads
 
+    if name == "c4" and args is not None and args.c4_points != 16_777_216:
+        return workloads.make("c4", n=args.c4_points, m=args.c4_points)
     return workloads.make(name)
 
 
@@ -252,7 +256,7 @@ def run_b200(args, world, rank, local):
     from torchbvh_b200 import _native
 
     device = torch.device("cuda", local)
-    w = load_workload(args.workload)
+    w = load_workload(args.workload, args)
     points = w.points.to(device)
     queries = w.queries.to(device)
     offsets = w.batch_offsets.to(device) if w.batch_offsets is not None else None
@@ -493,7 +497,7 @@ def cpu_baseline(w, args) -> dict:
 def run_reference(args, world, rank):
     if rank != 0:
         return None
-    w = load_workload(args.workload)
+    w = load_workload(args.workload, args)
     vals = []
     per_step_budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
     cpu = None
@@ -537,7 +541,7 @@ def run_reference_cuda(args, world, rank, local):
         import torchbvh as ref  # noqa: F401
     except Exception as exc:
         return {"impl": "reference_cuda", "unavailable": f"import failed: {exc}"}
-    w = load_workload(args.workload)
+    w = load_workload(args.workload, args)
     if w.k not in ref.SUPPORTED_K:
         return {"impl": "reference_cuda", "unavailable": f"k={w.k} not supported by the reference"}
     device = torch.device("cuda", local)
