@@ -83,7 +83,7 @@ int tbvh_build(int device, const float* points, int64_t num_clouds, int64_t poin
 /* ---------------------------------------------------------------------------
  * Morton permutation of query points. Replaces morton_sort_queries_narrow_cuda
  * (torchbvh/csrc/morton_sort.cu:264-287, bound as morton_sort_queries_narrow in
- * torchbvh/csrc/bindings.cpp:197). order_out[p] is the local query index of
+ * torchbvh/csrc/bindings.cpp:195). order_out[p] is the local query index of
  * the p-th query of its cloud in (Morton code, index) order, codes taken
  * against that cloud's scene_min/scene_max.
  */
@@ -113,7 +113,7 @@ int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clou
 /* ---------------------------------------------------------------------------
  * Exact k-NN. Replaces query_knn_batched_cached_bounds_cuda and
  * query_knn_batched_cached_bounds_ordered_cuda (torchbvh/csrc/knn_query.cu:
- * 419-446, bound in torchbvh/csrc/bindings.cpp:198-199) and, for ragged
+ * 419-446, bound in torchbvh/csrc/bindings.cpp:197-198) and, for ragged
  * input, the per-sample loop of _query_knn_ragged (torchbvh/_query.py:299-366).
  * order may be NULL (identity order, the unordered reference kernel).
  * Outputs: out_indices int64 [total_queries, k] (local source indices),
@@ -128,6 +128,26 @@ int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_in
                    int64_t total_queries, const int64_t* order, int dim, int k,
                    int64_t* out_indices, float* out_distances,
                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* tbvh_query_knn plus two options of the same traversal:
+ *  - source_points / out_positions (both or neither): also writes
+ *    out_positions[row, j, :] = source_points[cloud start + out_indices[row, j], :]
+ *    (float32 [total_queries, k, dim]) in the same kernel; replaces the
+ *    separate source_points[indices] / torch.gather of _query_knn_single /
+ *    _query_knn_batched (torchbvh/_query.py:174,203-215). An empty slot
+ *    (index -1, fewer than k reachable points) reads the cloud's last point.
+ *  - spatial_output = 1 (requires order): row = sorted (Morton) position
+ *    instead of the query's own row; replaces
+ *    query_knn_batched_cached_bounds_spatial_cuda (torchbvh/csrc/knn_query.cu:
+ *    448-461, bound in torchbvh/csrc/bindings.cpp:199). */
+int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                          int64_t num_clouds, int64_t points_per_cloud,
+                          const int64_t* point_offsets_dev, const int64_t* point_offsets_host,
+                          const float* queries, int64_t queries_per_cloud, const int64_t* query_offsets_dev,
+                          int64_t total_queries, const int64_t* order, int dim, int k,
+                          int64_t* out_indices, float* out_distances,
+                          const float* source_points, float* out_positions, int spatial_output,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -118,3 +118,36 @@ def test_workload_generators_are_seeded():
     sizes = r.cloud_sizes()
     assert len(sizes) == 8 and all(1024 <= s <= 4096 for s in sizes)
     assert torch.equal(r.points, r.queries)
+
+
+@pytest.mark.parametrize(
+    "pos_shape,q_shape,match",
+    [
+        ((24, 3), (2, 24, 3, 3), "pos.*shape"),
+        ((2, 24, 3), (2, 72, 3), "q.*shape"),
+        ((2, 24, 4), (2, 24, 3, 4), "D must be 2 or 3"),
+        ((1, 24, 3), (2, 24, 3, 3), "batch size"),
+        ((2, 24, 3), (2, 3, 3, 3), "point dimension"),
+        ((2, 24, 3), (2, 24, 3, 2), "last dimension"),
+        ((2, 24, 3), (2, 24, 0, 3), "at least one head"),
+        ((2, 24, 3), (2, 24, 3, 3), "CUDA tensor"),
+    ],
+)
+def test_displaced_validation_order_and_messages(pos_shape, q_shape, match):
+    with pytest.raises(ValueError, match=match):
+        torchbvh.query_displaced_knn(torch.zeros(pos_shape), torch.zeros(q_shape), 4)
+
+
+def test_interpolate_displaced_rejects_unknown_reduction_first():
+    with pytest.raises(ValueError, match="reduction must be 'weighted_mean'"):
+        torchbvh.interpolate_displaced(torch.zeros(1), torch.zeros(1), torch.zeros(1), 4, reduction="mean")
+
+
+def test_gather_neighbor_values_shape_checks_on_cpu():
+    values = torch.zeros((2, 6, 3, 4))
+    with pytest.raises(ValueError, match="values must have shape"):
+        torchbvh.gather_neighbor_values(values[0], torch.zeros((2, 6, 3, 2), dtype=torch.int64))
+    with pytest.raises(ValueError, match="head dimension"):
+        torchbvh.gather_neighbor_values(values, torch.zeros((2, 6, 2, 2), dtype=torch.int64))
+    with pytest.raises(ValueError, match="values must be a CUDA tensor"):
+        torchbvh.gather_neighbor_values(values, torch.zeros((2, 6, 3, 2), dtype=torch.int64))

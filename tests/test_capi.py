@@ -116,3 +116,23 @@ def test_sort_queries_rejects_bad_dim(native_lib):
 def test_empty_query_batch_is_a_no_op(native_lib):
     rc = native_lib.tbvh_query_knn(-1, 1, 1, 1, 64, None, None, 1, 0, 1, 0, None, 3, 4, 1, 1, None, 0, None)
     assert rc == _native.TBVH_OK
+
+
+def test_gather_rejects_source_without_positions(native_lib):
+    rc = native_lib.tbvh_query_knn_gather(-1, 1, 1, 1, 64, None, None, 1, 8, None, 8, None, 3, 4, 1, 1,
+                                          1, None, 0, None, 0, None)
+    assert rc == _native.TBVH_ERR_BAD_ARG
+    assert b"both" in native_lib.tbvh_last_error()
+
+
+def test_gather_rejects_spatial_without_order(native_lib):
+    rc = native_lib.tbvh_query_knn_gather(-1, 1, 1, 1, 64, None, None, 1, 8, None, 8, None, 3, 4, 1, 1,
+                                          None, None, 1, None, 0, None)
+    assert rc == _native.TBVH_ERR_BAD_ARG
+    assert b"spatial" in native_lib.tbvh_last_error()
+
+
+def test_gather_checks_the_same_arguments_as_query(native_lib):
+    rc = native_lib.tbvh_query_knn_gather(-1, 1, 1, 1, 64, None, None, 1, 8, None, 8, None, 3, 12, 1, 1,
+                                          1, 1, 0, None, 0, None)
+    assert rc == _native.TBVH_ERR_UNSUPPORTED_K

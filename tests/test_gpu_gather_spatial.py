@@ -1,0 +1,117 @@
+"""Fused neighbour-position gather and the spatial (sorted-row) output variant.
+
+The gather replaces the second pass ``source_points[indices]`` /
+``torch.gather`` of torchbvh/_query.py:174,203-215; the spatial variant is
+query_knn_batched_cached_bounds_spatial (torchbvh/csrc/knn_query.cu:448-461):
+row ``m`` of cloud ``b`` holds the neighbours of query ``query_order[b, m]``.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import torchbvh_b200 as torchbvh
+from torchbvh_b200._native import _C
+
+pytestmark = pytest.mark.gpu
+
+
+def _cloud(seed, shape):
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(shape, generator=g).cuda()
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+@pytest.mark.parametrize("k", [4, 8, 16, 32])
+@pytest.mark.parametrize("sort_queries", [True, False])
+def test_single_fused_positions_equal_indexing(dim, k, sort_queries):
+    points = _cloud(dim * 100 + k, (3000, dim))
+    queries = _cloud(dim * 100 + k + 1, (1700, dim))
+    bvh = torchbvh.build_bvh(points)
+    idx, dist, pos = torchbvh.query_knn(bvh, queries, k, source_points=points, sort_queries=sort_queries)
+    ref_idx, ref_dist = torchbvh.query_knn(bvh, queries, k, sort_queries=sort_queries)
+    assert torch.equal(idx, ref_idx) and torch.equal(dist, ref_dist)
+    assert pos.shape == (1700, k, dim)
+    assert torch.equal(pos, points[idx])
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+@pytest.mark.parametrize("k", [4, 16, 32])
+def test_batched_fused_positions_equal_gather(dim, k):
+    points = _cloud(7 + dim + k, (3, 2048, dim))
+    queries = _cloud(8 + dim + k, (3, 999, dim))
+    bvh = torchbvh.build_bvh(points)
+    idx, dist, pos = torchbvh.query_knn(bvh, queries, k, source_points=points)
+    assert pos.shape == (3, 999, k, dim)
+    expect = torch.gather(points, 1, idx.reshape(3, -1, 1).expand(-1, -1, dim)).reshape(3, 999, k, dim)
+    assert torch.equal(pos, expect)
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+def test_ragged_fused_positions_equal_indexing(dim):
+    counts = [300, 40, 1200, 16]
+    qcounts = [50, 5, 700, 33]
+    points = _cloud(11 + dim, (sum(counts), dim))
+    queries = _cloud(12 + dim, (sum(qcounts), dim))
+    offsets = torch.tensor(np.concatenate([[0], np.cumsum(counts)]), dtype=torch.int64, device="cuda")
+    qoffsets = torch.tensor(np.concatenate([[0], np.cumsum(qcounts)]), dtype=torch.int64, device="cuda")
+    bvh = torchbvh.build_bvh(points, batch_offsets=offsets)
+    idx, dist, pos = torchbvh.query_knn(bvh, queries, 8, query_offsets=qoffsets, source_points=points)
+    base = torch.repeat_interleave(offsets[:-1], torch.diff(qoffsets))
+    assert torch.equal(pos, points[idx + base[:, None]])
+
+
+@pytest.mark.parametrize("batched", [False, True])
+def test_fused_positions_gradient_matches_indexing(batched):
+    shape = (2, 500, 3) if batched else (500, 3)
+    qshape = (2, 300, 3) if batched else (300, 3)
+    base = _cloud(21, shape)
+    queries = _cloud(22, qshape)
+    bvh = torchbvh.build_bvh(base)
+    weights = _cloud(23, qshape[:-1] + (8, 3))
+
+    src = base.clone().requires_grad_(True)
+    idx, _, pos = torchbvh.query_knn(bvh, queries, 8, source_points=src)
+    assert pos.requires_grad
+    (pos * weights).sum().backward()
+
+    src_ref = base.clone().requires_grad_(True)
+    if batched:
+        ref_pos = torch.gather(src_ref, 1, idx.reshape(2, -1, 1).expand(-1, -1, 3)).reshape(pos.shape)
+    else:
+        ref_pos = src_ref[idx]
+    (ref_pos * weights).sum().backward()
+    torch.testing.assert_close(src.grad, src_ref.grad, rtol=1e-6, atol=1e-6)
+
+
+def test_fused_positions_without_grad_are_plain_tensors():
+    points = _cloud(31, (400, 3)).requires_grad_(True)
+    bvh = torchbvh.build_bvh(points.detach())
+    with torch.no_grad():
+        _, _, pos = torchbvh.query_knn(bvh, points.detach()[:50], 4, source_points=points)
+    assert not pos.requires_grad
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+@pytest.mark.parametrize("k", [4, 8, 16, 32])
+def test_spatial_rows_are_ordered_results_in_sorted_order(dim, k):
+    points = _cloud(40 + k + dim, (2, 3000, dim))
+    queries = _cloud(41 + k + dim, (2, 1500, dim))
+    bvh = torchbvh.build_bvh(points)
+    order = _C.morton_sort_queries_narrow(queries, bvh["scene_min"], bvh["scene_max"]).contiguous()
+    args = (bvh["node_aabbs"], bvh["sorted_indices"], queries, order, bvh["num_leaves"], bvh["num_real_nodes"],
+            dim, k)
+    s_idx, s_dist = _C.query_knn_batched_cached_bounds_spatial(*args)
+    o_idx, o_dist = _C.query_knn_batched_cached_bounds_ordered(*args)
+    rows = order.unsqueeze(-1).expand(-1, -1, k)
+    assert torch.equal(s_idx, torch.gather(o_idx, 1, rows))
+    assert torch.equal(s_dist, torch.gather(o_dist, 1, rows))
+
+
+def test_spatial_requires_an_order():
+    points = _cloud(50, (1, 64, 3))
+    bvh = torchbvh.build_bvh(points)
+    with pytest.raises(RuntimeError, match="spatial"):
+        _C.query_knn_batched_cached_bounds_spatial(bvh["node_aabbs"], bvh["sorted_indices"], points, None,
+                                                    bvh["num_leaves"], bvh["num_real_nodes"], 3, 4)

@@ -56,6 +56,11 @@ _SIGNATURES = {
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),
+    "tbvh_query_knn_gather": (
+        _i32,
+        [_i32, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i32, _i32, _ptr, _ptr, _ptr, _ptr,
+         _i32, _ptr, _size, _ptr],
+    ),
     "tbvh_query_knn": (
         _i32,
         [_i32, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i32, _i32, _ptr, _ptr, _ptr, _size,
@@ -281,7 +286,8 @@ def morton_sort_queries_ragged(queries: torch.Tensor, query_offsets: torch.Tenso
 # k-NN
 # ---------------------------------------------------------------------------
 
-def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_leaves, num_real_nodes, dim, k):
+def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_leaves, num_real_nodes, dim, k,
+                source_points=None, spatial=False):
     if dim not in (2, 3):
         raise RuntimeError(f"{op}: D must be 2 or 3")
     if not (query_points.is_cuda and query_points.is_contiguous() and query_points.dtype == torch.float32):
@@ -314,26 +320,36 @@ def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_l
         raise RuntimeError(f"{op}: all inputs must share a device")
     if k not in (4, 8, 16, 32):
         raise RuntimeError(f"{op}: k must be 4, 8, or 16 (or 32), got {k}")
+    if source_points is not None:
+        if not (source_points.is_cuda and source_points.is_contiguous() and source_points.dtype == torch.float32
+                and source_points.shape == (query_points.size(0), num_leaves, dim)
+                and source_points.device == device):
+            raise RuntimeError(f"{op}: source_points must be contiguous CUDA float32 of shape (B, N, D)")
     batch, m = int(query_points.size(0)), int(query_points.size(1))
     indices = torch.empty((batch, m, k), dtype=torch.int64, device=device)
     distances = torch.empty((batch, m, k), dtype=torch.float32, device=device)
+    positions = (torch.empty((batch, m, k, dim), dtype=torch.float32, device=device)
+                 if source_points is not None else None)
     if batch * m == 0:
-        return indices, distances
+        return (indices, distances) if positions is None else (indices, distances, positions)
     lib = load_library()
     hooks = _knn_hooks
     if hooks:
         for h in hooks:
             h("start", device)
-    _check(lib.tbvh_query_knn(
+    _check(lib.tbvh_query_knn_gather(
         device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), batch, int(num_leaves), None, None,
         query_points.data_ptr(), m, None, batch * m,
         query_order.data_ptr() if query_order is not None else None, dim, int(k),
-        indices.data_ptr(), distances.data_ptr(), None, 0, _stream(device),
+        indices.data_ptr(), distances.data_ptr(),
+        source_points.data_ptr() if source_points is not None else None,
+        positions.data_ptr() if positions is not None else None, 1 if spatial else 0,
+        None, 0, _stream(device),
     ))
     if hooks:
         for h in hooks:
             h("end", device)
-    return indices, distances
+    return (indices, distances) if positions is None else (indices, distances, positions)
 
 
 def query_knn_batched_cached_bounds(node_aabbs, sorted_indices, query_points, num_leaves, num_real_nodes, dim, k):
@@ -349,16 +365,37 @@ def query_knn_batched_cached_bounds_ordered(node_aabbs, sorted_indices, query_po
                        query_order, num_leaves, num_real_nodes, dim, k)
 
 
+def query_knn_batched_cached_bounds_spatial(node_aabbs, sorted_indices, query_points, query_order,
+                                            num_leaves, num_real_nodes, dim, k):
+    """Morton-ordered exact k-NN with outputs left in the sorted order (knn_query.cu:448-461):
+    row m of cloud b holds the neighbours of query ``query_order[b, m]``."""
+    return _query_impl("query_knn_batched_cached_bounds_spatial", node_aabbs, sorted_indices, query_points,
+                       query_order, num_leaves, num_real_nodes, dim, k, spatial=True)
+
+
+def query_knn_gather_positions(node_aabbs, sorted_indices, query_points, query_order, source_points,
+                               num_leaves, num_real_nodes, dim, k):
+    """Exact k-NN that also returns ``source_points`` gathered at the neighbour indices,
+    (B, M, k, D), from the same kernel (no reference counterpart: the reference gathers
+    in a second pass, torchbvh/_query.py:174,203-215)."""
+    op = ("query_knn_batched_cached_bounds_ordered" if query_order is not None
+          else "query_knn_batched_cached_bounds")
+    return _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_leaves, num_real_nodes,
+                       dim, k, source_points=source_points)
+
+
 def query_knn_ragged(packed: dict, query_points: torch.Tensor, query_offsets: torch.Tensor, total_queries: int,
-                     order: torch.Tensor | None, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+                     order: torch.Tensor | None, k: int, source_points: torch.Tensor | None = None):
     """Packed ragged exact k-NN over every cloud in one launch (no reference counterpart)."""
     dim = int(packed["dim"])
     device = query_points.device
     clouds = len(packed["point_offsets"]) - 1
     indices = torch.empty((total_queries, k), dtype=torch.int64, device=device)
     distances = torch.empty((total_queries, k), dtype=torch.float32, device=device)
+    positions = (torch.empty((total_queries, k, dim), dtype=torch.float32, device=device)
+                 if source_points is not None else None)
     if total_queries == 0:
-        return indices, distances
+        return (indices, distances) if positions is None else (indices, distances, positions)
     lib = load_library()
     host_offsets = (ctypes.c_int64 * (clouds + 1))(*packed["point_offsets"])
     ws = _workspace(lib.tbvh_query_knn_workspace_size(clouds, 0), device)
@@ -366,17 +403,20 @@ def query_knn_ragged(packed: dict, query_points: torch.Tensor, query_offsets: to
     if hooks:
         for h in hooks:
             h("start", device)
-    _check(lib.tbvh_query_knn(
+    _check(lib.tbvh_query_knn_gather(
         device.index, packed["node_aabbs"].data_ptr(), packed["sorted_indices"].data_ptr(), clouds, 0,
         packed["point_offsets_device"].data_ptr(), ctypes.cast(host_offsets, _ptr),
         query_points.data_ptr(), 0, query_offsets.data_ptr(), total_queries,
         order.data_ptr() if order is not None else None, dim, int(k),
-        indices.data_ptr(), distances.data_ptr(), ws.data_ptr(), ws.numel(), _stream(device),
+        indices.data_ptr(), distances.data_ptr(),
+        source_points.data_ptr() if source_points is not None else None,
+        positions.data_ptr() if positions is not None else None, 0,
+        ws.data_ptr(), ws.numel(), _stream(device),
     ))
     if hooks:
         for h in hooks:
             h("end", device)
-    return indices, distances
+    return (indices, distances) if positions is None else (indices, distances, positions)
 
 
 # Optional observers of the traversal launch (bench.py times the kernel with
@@ -388,6 +428,8 @@ _C = types.SimpleNamespace(
     morton_sort_queries_narrow=morton_sort_queries_narrow,
     query_knn_batched_cached_bounds=query_knn_batched_cached_bounds,
     query_knn_batched_cached_bounds_ordered=query_knn_batched_cached_bounds_ordered,
+    query_knn_batched_cached_bounds_spatial=query_knn_batched_cached_bounds_spatial,
+    query_knn_gather_positions=query_knn_gather_positions,
     build_bvh_ragged=build_bvh_ragged,
     morton_sort_queries_ragged=morton_sort_queries_ragged,
     query_knn_ragged=query_knn_ragged,

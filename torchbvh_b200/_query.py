@@ -164,20 +164,33 @@ def _query_knn_single(
     if query_points.device != data["sorted_indices"].device:
         raise ValueError("query_knn: query_points must be on the same device as the BVH")
     query_points = _as_contiguous(query_points)
+    if source_points is not None:
+        _validate_single_source_points("query_knn", data, source_points)
+        source_points = _as_contiguous(source_points)
     batched_queries = query_points.unsqueeze(0)
     node_aabbs = data["node_aabbs"].unsqueeze(0)
     sorted_indices = data["sorted_indices"].unsqueeze(0)
+    sort_perm = None
     if sort_queries:
         sort_perm = _C.morton_sort_queries_narrow(
             batched_queries,
             data["scene_min"].unsqueeze(0),
             data["scene_max"].unsqueeze(0),
+        ).contiguous()
+    if source_points is not None:
+        indices, squared_distances, positions = _C.query_knn_gather_positions(
+            node_aabbs, sorted_indices, batched_queries, sort_perm, source_points.detach().unsqueeze(0),
+            data["num_leaves"], data["num_real_nodes"], data["dim"], k,
         )
+        indices = indices.squeeze(0)
+        positions = _with_source_grad(source_points, positions.squeeze(0), indices, int(data["num_leaves"]))
+        return indices, squared_distances.squeeze(0), positions
+    if sort_queries:
         indices, squared_distances = _C.query_knn_batched_cached_bounds_ordered(
             node_aabbs,
             sorted_indices,
             batched_queries,
-            sort_perm.contiguous(),
+            sort_perm,
             data["num_leaves"],
             data["num_real_nodes"],
             data["dim"],
@@ -193,14 +206,54 @@ def _query_knn_single(
             data["dim"],
             k,
         )
-    indices = indices.squeeze(0)
-    squared_distances = squared_distances.squeeze(0)
-    if source_points is None:
-        return indices, squared_distances
+    return indices.squeeze(0), squared_distances.squeeze(0)
 
-    _validate_single_source_points("query_knn", data, source_points)
-    source_points = _as_contiguous(source_points)
-    return indices, squared_distances, source_points[indices]
+
+class _GatheredPositions(torch.autograd.Function):
+    """Neighbour positions gathered inside the k-NN kernel, differentiable with
+    respect to ``source_points`` like the reference's ``source_points[indices]``
+    (torchbvh/_query.py:174,203-215): the backward pass scatter-adds each
+    neighbour's gradient onto the source row it was read from."""
+
+    @staticmethod
+    def forward(ctx, source_points, positions, source_rows):
+        ctx.save_for_backward(source_rows)
+        ctx.source_shape = source_points.shape
+        return positions
+
+    @staticmethod
+    def backward(ctx, grad_positions):
+        (source_rows,) = ctx.saved_tensors
+        shape = ctx.source_shape
+        dim = shape[-1]
+        grad = torch.zeros((_rows_of(shape), dim), dtype=grad_positions.dtype, device=grad_positions.device)
+        grad.index_add_(0, source_rows.reshape(-1), grad_positions.reshape(-1, dim))
+        return grad.reshape(shape), None, None
+
+
+def _rows_of(shape) -> int:
+    rows = 1
+    for extent in shape[:-1]:
+        rows *= int(extent)
+    return rows
+
+
+def _with_source_grad(source_points, positions, indices, cloud_size, row_base=None):
+    """Attaches the gradient path to fused-gather positions when ``source_points``
+    requires it. ``cloud_size`` is each row's cloud point count (an int, or a
+    tensor broadcasting against ``indices``); ``row_base`` the first source row of
+    each query's cloud. An empty slot (-1) read the cloud's last point in the
+    kernel, so its gradient goes there too."""
+    if not (torch.is_grad_enabled() and source_points.requires_grad):
+        return positions
+    if isinstance(cloud_size, torch.Tensor):
+        last = cloud_size - 1
+    else:
+        last = torch.full_like(indices, cloud_size - 1)
+    rows = torch.where(indices < 0, last, indices)
+    if row_base is not None:
+        rows = rows + row_base
+    return _GatheredPositions.apply(source_points, positions, rows)
 
 
 def _validate_single_source_points(prefix: str, data: Mapping, source_points: torch.Tensor) -> None:
@@ -229,17 +282,6 @@ def _validate_batched_source_points(prefix: str, data: Mapping, source_points: t
         raise ValueError(f"{prefix}: source_points must be on the same device as the BVH")
 
 
-def _gather_batched_neighbor_positions(
-    source_points: torch.Tensor,
-    indices: torch.Tensor,
-    query_count: int,
-    dim: int,
-) -> torch.Tensor:
-    batch_size, _, neighbor_count = indices.shape
-    gather_index = indices.reshape(batch_size, query_count * neighbor_count, 1).expand(-1, -1, dim)
-    return torch.gather(source_points, 1, gather_index).reshape(batch_size, query_count, neighbor_count, dim)
-
-
 def _query_knn_batched(
     bvh: BatchedBVHHandle,
     query_points: torch.Tensor,
@@ -260,14 +302,28 @@ def _query_knn_batched(
     if query_points.device != data["sorted_indices"].device:
         raise ValueError("query_knn: query_points must be on the same device as the BVH")
     query_points = _as_contiguous(query_points)
+    if source_points is not None:
+        _validate_batched_source_points("query_knn", data, source_points)
+        source_points = _as_contiguous(source_points)
 
+    sort_perm = None
     if sort_queries:
-        sort_perm = _C.morton_sort_queries_narrow(query_points, data["scene_min"], data["scene_max"])
+        sort_perm = _C.morton_sort_queries_narrow(query_points, data["scene_min"], data["scene_max"]).contiguous()
+    if source_points is not None:
+        indices, squared_distances, positions = _C.query_knn_gather_positions(
+            data["node_aabbs"], data["sorted_indices"], query_points, sort_perm, source_points.detach(),
+            data["num_leaves"], data["num_real_nodes"], data["dim"], k,
+        )
+        n = int(data["num_leaves"])
+        cloud_base = (torch.arange(indices.size(0), device=indices.device, dtype=torch.int64) * n).view(-1, 1, 1)
+        positions = _with_source_grad(source_points, positions, indices, n, cloud_base)
+        return indices, squared_distances, positions
+    if sort_queries:
         indices, squared_distances = _C.query_knn_batched_cached_bounds_ordered(
             data["node_aabbs"],
             data["sorted_indices"],
             query_points,
-            sort_perm.contiguous(),
+            sort_perm,
             data["num_leaves"],
             data["num_real_nodes"],
             data["dim"],
@@ -283,15 +339,7 @@ def _query_knn_batched(
             data["dim"],
             k,
         )
-    if source_points is None:
-        return indices, squared_distances
-
-    _validate_batched_source_points("query_knn", data, source_points)
-    source_points = _as_contiguous(source_points)
-    neighbor_positions = _gather_batched_neighbor_positions(
-        source_points, indices, query_points.size(1), int(data["dim"])
-    )
-    return indices, squared_distances, neighbor_positions
+    return indices, squared_distances
 
 
 def _validate_ragged_source_points(
@@ -360,12 +408,17 @@ def _query_knn_ragged(
 
     total = q_offsets[-1]
     order = _C.morton_sort_queries_ragged(query_points, query_offsets, total, packed["scene_min"], packed["scene_max"])
-    indices, distances = _C.query_knn_ragged(packed, query_points, query_offsets, total, order, k)
     if source_points is None:
-        return indices, distances
-    query_counts = torch.diff(query_offsets)
-    row_base = torch.repeat_interleave(packed["point_offsets_device"][:-1], query_counts, output_size=total)
-    positions = source_points[indices + row_base[:, None]]
+        return _C.query_knn_ragged(packed, query_points, query_offsets, total, order, k)
+    indices, distances, positions = _C.query_knn_ragged(
+        packed, query_points, query_offsets, total, order, k, source_points=source_points.detach()
+    )
+    if torch.is_grad_enabled() and source_points.requires_grad:
+        query_counts = torch.diff(query_offsets)
+        point_offsets = packed["point_offsets_device"]
+        row_base = torch.repeat_interleave(point_offsets[:-1], query_counts, output_size=total)[:, None]
+        sizes = torch.repeat_interleave(torch.diff(point_offsets), query_counts, output_size=total)[:, None]
+        positions = _with_source_grad(source_points, positions, indices, sizes, row_base)
     return indices, distances, positions
 
 

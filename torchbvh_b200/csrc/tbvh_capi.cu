@@ -269,14 +269,21 @@ size_t tbvh_query_knn_workspace_size(int64_t num_clouds, int64_t points_per_clou
   return align_up(size_t(num_clouds) * sizeof(tbvh::CloudTree), 256);
 }
 
-int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_indices,
-                   int64_t num_clouds, int64_t points_per_cloud,
-                   const int64_t* point_offsets_dev, const int64_t* point_offsets_host,
-                   const float* queries, int64_t queries_per_cloud, const int64_t* query_offsets_dev,
-                   int64_t total_queries, const int64_t* order, int dim, int k,
-                   int64_t* out_indices, float* out_distances,
-                   void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = order ? "query_knn_batched_cached_bounds_ordered" : "query_knn_batched_cached_bounds";
+int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                          int64_t num_clouds, int64_t points_per_cloud,
+                          const int64_t* point_offsets_dev, const int64_t* point_offsets_host,
+                          const float* queries, int64_t queries_per_cloud, const int64_t* query_offsets_dev,
+                          int64_t total_queries, const int64_t* order, int dim, int k,
+                          int64_t* out_indices, float* out_distances,
+                          const float* source_points, float* out_positions, int spatial_output,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = spatial_output ? "query_knn_batched_cached_bounds_spatial"
+                   : order        ? "query_knn_batched_cached_bounds_ordered"
+                                  : "query_knn_batched_cached_bounds";
+  if ((source_points == nullptr) != (out_positions == nullptr))
+    return fail(TBVH_ERR_BAD_ARG, "%s: source_points and out_positions must both be given or both be NULL", op);
+  if (spatial_output && order == nullptr)
+    return fail(TBVH_ERR_BAD_ARG, "%s: spatial output needs a query order", op);
   g_last_error.clear();
   if (dim != 2 && dim != 3) return fail(TBVH_ERR_BAD_ARG, "%s: D must be 2 or 3", op);
   if (k != 4 && k != 8 && k != 16 && k != 32)
@@ -321,9 +328,25 @@ int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_in
   q.total_queries = total_queries;
   q.dim = dim;
   q.k = k;
+  q.source_points = source_points;
+  q.out_positions = out_positions;
+  q.spatial = spatial_output != 0;
   cudaError_t e = tbvh::launch_knn(q, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, op);
   return TBVH_OK;
+}
+
+int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                   int64_t num_clouds, int64_t points_per_cloud,
+                   const int64_t* point_offsets_dev, const int64_t* point_offsets_host,
+                   const float* queries, int64_t queries_per_cloud, const int64_t* query_offsets_dev,
+                   int64_t total_queries, const int64_t* order, int dim, int k,
+                   int64_t* out_indices, float* out_distances,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  return tbvh_query_knn_gather(device, node_aabbs, sorted_indices, num_clouds, points_per_cloud,
+                               point_offsets_dev, point_offsets_host, queries, queries_per_cloud,
+                               query_offsets_dev, total_queries, order, dim, k, out_indices, out_distances,
+                               nullptr, nullptr, 0, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

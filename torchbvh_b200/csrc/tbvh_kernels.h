@@ -110,6 +110,9 @@ struct KnnLaunch {
   int64_t total_queries;
   int dim;
   int k;
+  const float* source_points = nullptr;  // fused neighbour-position gather (nullable)
+  float* out_positions = nullptr;
+  bool spatial = false;                  // output rows in sorted order
 };
 
 cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream);

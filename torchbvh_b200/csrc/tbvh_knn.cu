@@ -58,6 +58,9 @@ struct KnnArgs {
   CloudTree uni;
   int64_t uni_rows;
   int64_t total_q;
+  const float* src_points;  // nullable: fused neighbour-position gather source
+  float* out_pos;           // nullable: (rows, K, D) neighbour positions
+  int spatial;              // 1: write row = sorted (Morton) position, else the query's own row
   unsigned* status;
 };
 
@@ -371,8 +374,11 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   (void)nd;
 
   if (mine) {
-    int64_t* oi = a.out_idx + gq * K;
-    float* od = a.out_dist + gq * K;
+    // Output row: the query's own row, or its position in the sorted order
+    // (the reference's spatial variant, knn_query.cu:448-461).
+    const int64_t row = a.spatial ? pos : gq;
+    int64_t* oi = a.out_idx + row * K;
+    float* od = a.out_dist + row * K;
 #pragma unroll
     for (int i = 0; i < K; i += 2) {
       reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(key[i]), key_idx(key[i + 1]));
@@ -381,6 +387,19 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     for (int i = 0; i < K; i += 4) {
       reinterpret_cast<float4*>(od)[i / 4] =
           make_float4(key_dist(key[i]), key_dist(key[i + 1]), key_dist(key[i + 2]), key_dist(key[i + 3]));
+    }
+    if (a.out_pos) {
+      // Fused source_points[indices] gather. An empty slot (index -1) reads the
+      // cloud's last point, as PyTorch's negative indexing would.
+      const float* src = a.src_points + pt_off * D;
+      float* op = a.out_pos + row * K * D;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        int64_t idx = key_idx(key[i]);
+        if (idx < 0) idx = n - 1;
+#pragma unroll
+        for (int c = 0; c < D; ++c) op[i * D + c] = __ldg(src + idx * D + c);
+      }
     }
   }
 }
@@ -467,6 +486,9 @@ cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream) {
   a.uni = q.uniform;
   a.uni_rows = q.uniform_rows;
   a.total_q = q.total_queries;
+  a.src_points = q.source_points;
+  a.out_pos = q.out_positions;
+  a.spatial = q.spatial ? 1 : 0;
   a.status = device_status_ptr();
   if (q.points.uniform_n > 0) {
     a.table = nullptr;
