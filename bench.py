@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--c4-points", type=int, default=16_777_216,
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
+    ap.add_argument("--c4-split", default="morton", choices=["morton", "contiguous"],
+                    help="c4 on N > 1 GPUs: share of the queries per rank (a range of their Morton order, "
+                         "or of their given order)")
     ap.add_argument("--cpu-sample-queries", type=int, default=0,
                     help="queries per sampled cloud for the CPU baseline (0 = automatic)")
     return ap.parse_args()
@@ -279,8 +282,13 @@ def run_b200(args, world, rank, local):
         ev.record(torch.cuda.current_stream(dev))
         knn_events.append((phase, ev))
 
+    # Warm-up holds references the way the timed loop does (the previous step's
+    # BVH and results stay alive while the next step runs), so the caching
+    # allocator has grown to its steady state before timing starts; otherwise
+    # the second timed step pays for new device segments.
+    bvh = out = None
     for _ in range(args.warmup):
-        step(points, queries, offsets, qoffsets)
+        bvh, out = step(points, queries, offsets, qoffsets)
     torch.cuda.synchronize(device)
     assert torchbvh.device_status(device) == 0
 
@@ -418,6 +426,152 @@ def run_b200(args, world, rank, local):
         "gpu": torch.cuda.get_device_name(device),
     }
     return result
+
+
+def run_b200_single_cloud_sharded(args, world, rank, local):
+    """c4 on N > 1 GPUs, the sharded single-cloud form (strong scaling).
+
+    One step: rank 0's points are broadcast (NCCL), every rank builds the same
+    BVH, sorts all queries by Morton code against it, takes its range of that
+    order and queries it; the results stay on the rank that computed them
+    (`value`). `all_gather` times the same step followed by the all-gather of
+    every result row into the original query order on every rank.
+    """
+    import torchbvh_b200 as torchbvh
+    from torchbvh_b200 import _native
+    from torchbvh_b200 import distributed as tdist
+
+    device = torch.device("cuda", local)
+    w = load_workload("c4", args)
+    n, m, dim, k = w.num_points, w.num_queries, w.dim, w.k
+    points = w.points.to(device) if rank == 0 else None
+    queries = w.queries.to(device)
+
+    def step(p, q, gather):
+        return tdist.knn_sharded_single_cloud(p, q, k, num_points=n, dim=dim, gather=gather,
+                                              split=args.c4_split, device=device)
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    knn_events: list = []
+
+    def hook(phase, dev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        knn_events.append((phase, ev))
+
+    def timed(gather, steps, warmup, inputs):
+        out = None
+        for _ in range(warmup):
+            out = step(*inputs(), gather)
+        torch.cuda.synchronize(device)
+        barrier(world)
+        launches0 = _native.load_library().tbvh_kernel_launch_count()
+        ev = []
+        for _ in range(steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = step(*inputs(), gather)
+            b.record(stream)
+            ev.append((a, b))
+        torch.cuda.synchronize(device)
+        del out
+        launches = _native.load_library().tbvh_kernel_launch_count() - launches0
+        return sum(a.elapsed_time(b) for a, b in ev), launches
+
+    resident = lambda: (points, queries)  # noqa: E731
+    _native._knn_hooks.append(hook)
+    sampler = ClockSampler(local)
+    with sampler:
+        total_ms, launches = timed("none", args.steps, args.warmup, resident)
+    _native._knn_hooks.remove(hook)
+    total_ms_max = max_over_ranks(total_ms, world)
+    starts = [e for ph, e in knn_events if ph == "start"][-args.steps:]
+    ends = [e for ph, e in knn_events if ph == "end"][-args.steps:]
+    knn_avg_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / len(starts), world)
+
+    gather_steps = max(3, min(args.steps, 10))
+    gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
+    status = torchbvh.device_status(device)
+
+    e2e = None
+    if not args.no_e2e:
+        hp = w.points.pin_memory() if rank == 0 else None
+        hq = w.queries.pin_memory()
+        q0, q1 = tdist.shard_range(m, world, rank)
+        host_idx = torch.empty((q1 - q0, k), dtype=torch.int64).pin_memory()
+        host_dist = torch.empty((q1 - q0, k), dtype=torch.float32).pin_memory()
+
+        def e2e_inputs():
+            p = hp.to(device, non_blocking=True) if rank == 0 else None
+            return p, hq.to(device, non_blocking=True)
+
+        def e2e_step_ms(steps):
+            ev = []
+            for i in range(steps + 2):
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                idx, dist_sq, _ = step(*e2e_inputs(), "none")
+                host_idx.copy_(idx, non_blocking=True)
+                host_dist.copy_(dist_sq, non_blocking=True)
+                b.record(stream)
+                if i >= 2:
+                    ev.append((a, b))
+            torch.cuda.synchronize(device)
+            return sum(a.elapsed_time(b) for a, b in ev)
+
+        e2e_steps = max(3, min(args.steps, 10))
+        e2e_ms = max_over_ranks(e2e_step_ms(e2e_steps), world)
+        e2e = {"value": m * e2e_steps / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": (n * dim * 4 if rank == 0 else 0) + m * dim * 4,
+               "d2h_bytes_per_step": (q1 - q0) * k * 12,
+               "ms_per_step": e2e_ms / e2e_steps,
+               "api": "torchbvh_b200.distributed.knn_sharded_single_cloud(..., gather='none') from pinned host "
+                      "buffers (byte counts of rank 0)"}
+
+    from torchbvh_b200 import workloads
+
+    share = -(-m // world)
+    _, query_bytes = workloads.algorithmic_bytes([n], [share], dim, k)
+    peak, peak_kind = measured_peak_hbm()
+    achieved = query_bytes / (knn_avg_ms / 1e3) / 1e9
+    return {
+        "metric": METRIC,
+        "value": m * args.steps / (total_ms_max / 1e3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded CPU generator, torchbvh_b200.workloads)",
+        "config": {**workload_config(w, world),
+                   "parallelism": (f"points broadcast from rank 0 (NCCL), BVH built on each of {world} GPUs, "
+                                   f"queries split by {'Morton-order' if args.c4_split == 'morton' else 'index'} "
+                                   f"range, results left on the computing rank")},
+        "all_gather": {"value": m * gather_steps / (gather_ms / 1e3), "unit": UNIT,
+                       "ms_per_step": gather_ms / gather_steps,
+                       "note": "same step plus the all-gather of all (M, k) result rows into query order"},
+        "knn_kernel_ms": knn_avg_ms,
+        "roofline": {"kernel": "k_knn (warp-packet BVH traversal), one rank's share", "bound": "hbm",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,
+                     "algorithmic_bytes_per_launch": query_bytes, "avg_launch_ms": knn_avg_ms},
+        "cpu_baseline": None,
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps,
+        "device_status": status,
+        "clocks": sampler.summary(),
+        "gpu": torch.cuda.get_device_name(device),
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -587,6 +741,8 @@ def main():
             result = run_reference(args, world, rank)
         elif args.impl == "reference_cuda":
             result = run_reference_cuda(args, world, rank, local)
+        elif args.workload == "c4" and world > 1:
+            result = run_b200_single_cloud_sharded(args, world, rank, local)
         else:
             result = run_b200(args, world, rank, local)
         if rank == 0 and result is not None:

@@ -41,6 +41,16 @@ def oracle_knn(points, queries, k, *, batch_offsets=None, query_offsets=None):
     return torch.from_numpy(i), torch.from_numpy(d)
 
 
+def oracle_order(points, queries):
+    """Morton order of the queries against the points' bounding box (the CPU oracle's codes)."""
+    from oracle import pyoracle
+
+    lo = points.min(0).values.numpy()
+    hi = points.max(0).values.numpy()
+    codes = pyoracle.morton_codes(queries.numpy(), lo, hi)
+    return torch.from_numpy(pyoracle.stable_argsort(codes).astype(np.int64))
+
+
 def _data():
     g = torch.Generator().manual_seed(5)
     single_p = torch.rand((700, 3), generator=g)
@@ -70,9 +80,15 @@ def _worker(rank, world, port, outdir, mode):
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected host-side failure on rank 1")
         out["single_all"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 8, num_points=700, dim=3,
-                                                           knn_fn=oracle_knn)
+                                                           split="contiguous", knn_fn=oracle_knn)
         out["single_root"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 4, num_points=700, dim=3,
-                                                            gather="root", knn_fn=oracle_knn)
+                                                            gather="root", split="contiguous", knn_fn=oracle_knn)
+        out["morton_all"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 8, num_points=700, dim=3,
+                                                           order_fn=oracle_order, knn_fn=oracle_knn)
+        out["morton_root"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 4, num_points=700, dim=3,
+                                                            gather="root", order_fn=oracle_order, knn_fn=oracle_knn)
+        out["morton_none"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 4, num_points=700, dim=3,
+                                                            gather="none", order_fn=oracle_order, knn_fn=oracle_knn)
         out["batched"] = tdist.knn_sharded_batched(bp, bq, 4, knn_fn=oracle_knn)
         out["ragged"] = tdist.knn_sharded_ragged(rp, bo, rq, qo, 4, knn_fn=oracle_knn)
         torch.save(out, Path(outdir) / f"rank{rank}.pt")
@@ -128,6 +144,18 @@ def test_sharded_paths_match_single_process():
     ei4, ed4 = oracle_knn(sp, sq, 4)
     assert torch.equal(r0["single_root"][0], ei4) and torch.equal(r0["single_root"][1], ed4)
     assert r1["single_root"] == (None, None)
+    # Morton split: same results in the original query order; the shares are
+    # consecutive ranges of the Morton order and cover every query once.
+    for r in (r0, r1):
+        assert torch.equal(r["morton_all"][0], ei) and torch.equal(r["morton_all"][1], ed)
+    assert torch.equal(r0["morton_root"][0], ei4) and torch.equal(r0["morton_root"][1], ed4)
+    assert r1["morton_root"] == (None, None)
+    order = oracle_order(sp, sq)
+    owned = torch.cat([r0["morton_none"][2], r1["morton_none"][2]])
+    assert torch.equal(owned, order)
+    for r in (r0, r1):
+        i, d, rows = r["morton_none"]
+        assert torch.equal(i, ei4[rows]) and torch.equal(d, ed4[rows])
     bi, bd = oracle_knn(bp, bq, 4)
     ri, rd = oracle_knn(rp, rq, 4, batch_offsets=torch.tensor(bo), query_offsets=torch.tensor(qo))
     for r in (r0, r1):

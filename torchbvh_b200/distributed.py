@@ -5,8 +5,13 @@ input shapes:
 
 * ``knn_sharded_single_cloud``: one large cloud. Rank ``src`` holds the
   points; they are broadcast (NCCL over NVLink), every rank builds the same
-  BVH, takes a contiguous slice of the queries, queries it, and the result
-  slices are all-gathered (or gathered to ``src``).
+  BVH, takes its share of the queries, queries it, and the result slices are
+  all-gathered (or gathered to ``src``, or left where they were computed).
+  The share is a contiguous range of the queries' Morton order
+  (``split="morton"``, the default) or of their given order
+  (``split="contiguous"``): Morton ranges keep each warp's 32 queries
+  spatially close and each rank's walk to one region of the tree, where a
+  slice of randomly ordered queries spreads every warp over the whole cloud.
 * ``knn_sharded_batched``: fixed-size batches, clouds split contiguously over
   ranks, results all-gathered in cloud order.
 * ``knn_sharded_ragged``: ragged batches, clouds assigned by a size-balanced
@@ -75,16 +80,39 @@ def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Ten
     return torch.cat([b[:c] for b, c in zip(bufs, counts)])
 
 
+def _morton_share_cuda(points: torch.Tensor, queries: torch.Tensor, k: int, q0: int, q1: int):
+    """One BVH build; the queries' Morton order against its scene box; k-NN of
+    sorted positions [q0, q1) with the slice already in traversal order."""
+    from ._bvh_class import BVH
+    from ._native import _C
+
+    with BVH(points) as bvh:
+        h = bvh._handle
+        order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                              h["scene_max"].unsqueeze(0))[0]
+        mine = order[q0:q1]
+        idx, dist_sq = bvh.knn(queries.index_select(0, mine), k, sort_queries=False)
+    return order, mine, idx, dist_sq
+
+
 def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor, k: int, *,
                              num_points: int, dim: int, src: int = 0, group=None, gather: str = "all",
+                             split: str = "morton", order_fn: Callable | None = None,
                              knn_fn: KnnFn = default_knn, device: torch.device | None = None):
     """Exact k-NN of one cloud with the queries split over ranks.
 
     `points` is read on rank `src` only (other ranks may pass None); every rank
-    passes the full `queries` tensor (or a tensor with at least its own slice).
-    `gather`: "all" returns the full (M, k) results on every rank, "root" only
-    on `src` (None elsewhere), "none" returns this rank's slice and its range.
+    passes the full `queries` tensor. `split`: "morton" gives each rank a
+    contiguous range of the queries' Morton order (computed on every rank
+    against the shared BVH, or by `order_fn(points, queries)` when given),
+    "contiguous" a contiguous range of the given order. `gather`: "all"
+    returns the full (M, k) results in the original query order on every rank,
+    "root" only on `src` (None elsewhere), "none" returns this rank's rows and
+    which queries they belong to (the (start, end) range for "contiguous", the
+    int64 query indices for "morton").
     """
+    if split not in ("morton", "contiguous"):
+        raise ValueError("knn_sharded_single_cloud: split must be 'morton' or 'contiguous'")
     world, rank = _world(group)
     dev = device or queries.device
     buf = points if rank == src else torch.empty((num_points, dim), dtype=torch.float32, device=dev)
@@ -92,15 +120,37 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     dist.broadcast(buf, src=src, group=group)
     m = queries.shape[0]
     q0, q1 = shard_range(m, world, rank)
-    idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
+    order = None
+    if split == "contiguous":
+        idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
+        owned = (q0, q1)
+    elif order_fn is None and knn_fn is default_knn:
+        order, owned, idx, dist_sq = _morton_share_cuda(buf, queries, k, q0, q1)
+    else:
+        order = order_fn(buf, queries) if order_fn is not None else _morton_share_cuda(buf, queries, k, 0, 0)[0]
+        owned = order[q0:q1]
+        idx, dist_sq = knn_fn(buf, queries.index_select(0, owned).contiguous(), k)
     if gather == "none":
-        return idx, dist_sq, (q0, q1)
+        return idx, dist_sq, owned
     counts = [shard_range(m, world, r)[1] - shard_range(m, world, r)[0] for r in range(world)]
     if gather == "root":
         idx_all = _gather_to(idx, counts, src, group)
         dist_all = _gather_to(dist_sq, counts, src, group)
-        return (idx_all, dist_all) if rank == src else (None, None)
-    return _all_gather_rows(idx, counts, group), _all_gather_rows(dist_sq, counts, group)
+        if rank != src:
+            return None, None
+        return _to_query_order(idx_all, order), _to_query_order(dist_all, order)
+    idx_all = _all_gather_rows(idx, counts, group)
+    dist_all = _all_gather_rows(dist_sq, counts, group)
+    return _to_query_order(idx_all, order), _to_query_order(dist_all, order)
+
+
+def _to_query_order(rows: torch.Tensor, order: torch.Tensor | None) -> torch.Tensor:
+    """Rows in split order -> rows in query order (row p of `rows` belongs to query order[p])."""
+    if order is None:
+        return rows
+    out = torch.empty_like(rows)
+    out.index_copy_(0, order.to(rows.device), rows)
+    return out
 
 
 def _gather_to(local: torch.Tensor, counts: list[int], dst: int, group) -> torch.Tensor | None:
