@@ -490,7 +490,12 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
     total_ms_max = max_over_ranks(total_ms, world)
     starts = [e for ph, e in knn_events if ph == "start"][-args.steps:]
     ends = [e for ph, e in knn_events if ph == "end"][-args.steps:]
-    knn_avg_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / len(starts), world)
+    knn_local_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / len(starts)
+    knn_avg_ms = max_over_ranks(knn_local_ms, world)
+    import torch.distributed as dist
+
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps})
 
     gather_steps = max(3, min(args.steps, 10))
     gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
@@ -560,6 +565,7 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
                        "ms_per_step": gather_ms / gather_steps,
                        "note": "same step plus the all-gather of all (M, k) result rows into query order"},
         "knn_kernel_ms": knn_avg_ms,
+        "per_rank_ms": per_rank,
         "roofline": {"kernel": "k_knn (warp-packet BVH traversal), one rank's share", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "traffic": None,

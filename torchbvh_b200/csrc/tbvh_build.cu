@@ -273,7 +273,6 @@ __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, Clo
   }
   __syncthreads();
   const unsigned lane = lane_id();
-  const unsigned lt_mask = (1u << lane) - 1u;
   const int64_t rounds = (n + int64_t(gridDim.x) * blockDim.x - 1) / (int64_t(gridDim.x) * blockDim.x);
   int cur = -1;
   int64_t cur_end = -1;
@@ -305,10 +304,17 @@ __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, Clo
       code = morton_code<D>(p, lo, hi);
       keys[i] = code;
     }
+    // Digits of Morton codes in input order are mostly distinct within a warp,
+    // so each lane adds its own count; only a digit the whole warp shares (the
+    // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
     for (int ps = 0; ps < passes; ++ps) {
       const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
-      const unsigned peers = __match_any_sync(kFullMask, d);
-      if (d < 0x100u && (peers & lt_mask) == 0u) atomicAdd(&s_hist[ps][d], uint32_t(__popc(peers)));
+      const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
+      if (__all_sync(kFullMask, d == d0)) {
+        if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);
+      } else if (d < 0x100u) {
+        atomicAdd(&s_hist[ps][d], 1u);
+      }
     }
   }
   __syncthreads();

@@ -180,9 +180,11 @@ struct CloudMap {
   __device__ __forceinline__ int64_t size(int b) const {
     return uniform_n > 0 ? uniform_n : offsets[b + 1] - offsets[b];
   }
-  // Cloud that owns packed element e (0 <= e < total).
+  // Cloud that owns packed element e (0 <= e < total). Totals are below 2^31
+  // (checked by the host entry points), so the uniform case divides in 32 bits.
   __device__ __forceinline__ int find(int64_t e) const {
-    if (uniform_n > 0) return static_cast<int>(e / uniform_n);
+    if (num_clouds == 1) return 0;
+    if (uniform_n > 0) return static_cast<int>(uint32_t(e) / uint32_t(uniform_n));
     int lo = 0, hi = num_clouds - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
