@@ -447,9 +447,9 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
     points = w.points.to(device) if rank == 0 else None
     queries = w.queries.to(device)
 
-    def step(p, q, gather):
+    def step(p, q, gather, out=None):
         return tdist.knn_sharded_single_cloud(p, q, k, num_points=n, dim=dim, gather=gather,
-                                              split=args.c4_split, device=device)
+                                              split=args.c4_split, device=device, out=out)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
@@ -460,10 +460,10 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         ev.record(torch.cuda.current_stream(dev))
         knn_events.append((phase, ev))
 
-    def timed(gather, steps, warmup, inputs):
+    def timed(gather, steps, warmup, inputs, peer=None):
         out = None
         for _ in range(warmup):
-            out = step(*inputs(), gather)
+            out = step(*inputs(), gather, peer)
         torch.cuda.synchronize(device)
         barrier(world)
         launches0 = _native.load_library().tbvh_kernel_launch_count()
@@ -473,7 +473,7 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            out = step(*inputs(), gather)
+            out = step(*inputs(), gather, peer)
             b.record(stream)
             ev.append((a, b))
         torch.cuda.synchronize(device)
@@ -498,7 +498,9 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
     dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps})
 
     gather_steps = max(3, min(args.steps, 10))
-    gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
+    nccl_gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
+    with tdist.PeerResults(m, k, device=device) as peer:
+        gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident, peer)[0], world)
     status = torchbvh.device_status(device)
 
     e2e = None
@@ -563,7 +565,10 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
                                    f"range, results left on the computing rank")},
         "all_gather": {"value": m * gather_steps / (gather_ms / 1e3), "unit": UNIT,
                        "ms_per_step": gather_ms / gather_steps,
-                       "note": "same step plus the all-gather of all (M, k) result rows into query order"},
+                       "note": ("same step with every (M, k) result row delivered to every rank in query order: "
+                                "the traversal writes each row into all ranks' buffers over NVLink as it "
+                                "finishes (tbvh_query_knn_share)"),
+                       "nccl_all_gather_ms_per_step": nccl_gather_ms / gather_steps},
         "knn_kernel_ms": knn_avg_ms,
         "per_rank_ms": per_rank,
         "roofline": {"kernel": "k_knn (warp-packet BVH traversal), one rank's share", "bound": "hbm",

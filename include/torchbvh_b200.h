@@ -149,6 +149,41 @@ int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* so
                           const float* source_points, float* out_positions, int spatial_output,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * One cloud sharded over the GPUs of a node, results delivered to every GPU.
+ * No counterpart in the reference, which is single-GPU; this is the exchange
+ * step of the broadcast + split + all-gather form of one large cloud.
+ *
+ * Buffers that other GPUs write into are shared with CUDA IPC:
+ * tbvh_peer_alloc allocates `bytes` on `device` (cudaMalloc) and fills
+ * out_handle (tbvh_peer_handle_bytes() bytes) for the other processes;
+ * tbvh_peer_open maps such a handle on `device` (point-to-point mapping, no
+ * multicast); tbvh_peer_close / tbvh_peer_free undo them. Synchronous.
+ */
+size_t tbvh_peer_handle_bytes(void);
+int tbvh_peer_alloc(int device, size_t bytes, void** out_ptr, void* out_handle);
+int tbvh_peer_free(int device, void* ptr);
+int tbvh_peer_open(int device, const void* handle, void** out_ptr);
+int tbvh_peer_close(int device, void* ptr);
+
+/* Exact k-NN of this rank's share of the queries of one cloud (the BVH of
+ * num_points points built by tbvh_build), with every result row written into
+ * each of the num_dest (<= 8) destination buffers at the query's own row:
+ * dest_indices[d] int64 [num_queries, k], dest_distances[d] float32
+ * [num_queries, k], local or peer-mapped. `order` lists the share_count query
+ * indices (into `queries`, [num_queries, dim]) this rank serves, normally a
+ * contiguous range of their Morton order. Rows of other ranks' shares are not
+ * touched. Remote rows are NVLink stores made as the traversal finishes each
+ * query; the kernel ends with a system-scope fence, so a collective enqueued
+ * after it on every rank (a barrier) orders all deliveries before any rank
+ * reads its buffer. Callers must also order each rank's reads of the previous
+ * results before the next call's writes (a collective at the start of the
+ * step does). */
+int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
+                         const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
+                         int dim, int k, int num_dest, int64_t* const* dest_indices,
+                         float* const* dest_distances, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -136,3 +136,37 @@ def test_gather_checks_the_same_arguments_as_query(native_lib):
     rc = native_lib.tbvh_query_knn_gather(-1, 1, 1, 1, 64, None, None, 1, 8, None, 8, None, 3, 12, 1, 1,
                                           1, 1, 0, None, 0, None)
     assert rc == _native.TBVH_ERR_UNSUPPORTED_K
+
+
+def test_peer_handle_is_a_cuda_ipc_handle(native_lib):
+    assert native_lib.tbvh_peer_handle_bytes() == 64
+
+
+def _share(native_lib, **kw):
+    args = dict(device=-1, nodes=1, sorted=1, n=64, queries=1, m=16, order=1, count=16, dim=3, k=4,
+                ndest=1, didx=None, ddist=None)
+    args.update(kw)
+    ptrs = (ctypes.c_void_p * 8)(*([1] * 8))
+    didx = args["didx"] if args["didx"] is not None else ptrs
+    ddist = args["ddist"] if args["ddist"] is not None else ptrs
+    return native_lib.tbvh_query_knn_share(args["device"], args["nodes"], args["sorted"], args["n"], args["queries"],
+                                           args["m"], args["order"], args["count"], args["dim"], args["k"],
+                                           args["ndest"], didx, ddist, None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    ({"dim": 4}, "BAD_ARG"), ({"k": 12}, "UNSUPPORTED_K"), ({"n": 2}, "BAD_ARG"),
+    ({"count": 17}, "BAD_ARG"), ({"count": -1}, "BAD_ARG"), ({"ndest": 0}, "BAD_ARG"), ({"ndest": 9}, "BAD_ARG"),
+])
+def test_share_rejects_bad_arguments(native_lib, kw, code):
+    assert _share(native_lib, **kw) == getattr(_native, "TBVH_ERR_" + code)
+
+
+def test_share_rejects_null_destination(native_lib):
+    ptrs = (ctypes.c_void_p * 8)(1, None, 1, 1, 1, 1, 1, 1)
+    assert _share(native_lib, ndest=2, didx=ptrs) == _native.TBVH_ERR_BAD_ARG
+    assert b"destination" in native_lib.tbvh_last_error()
+
+
+def test_empty_share_is_a_no_op(native_lib):
+    assert _share(native_lib, count=0) == _native.TBVH_OK

@@ -66,6 +66,15 @@ def _worker(rank, world, port, outdir):
         i, d, rows = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, big_q.to(dev), 32,
                                                     num_points=big_p.shape[0], dim=3, device=dev, gather="none")
         out["single_none"] = (i.cpu(), d.cpu(), rows.cpu())
+        # Fused all-gather: each rank's traversal writes its rows into both
+        # ranks' buffers over NVLink; the same buffers serve consecutive calls.
+        peer = tdist.PeerResults(big_q.shape[0], 32, device=dev)
+        for rep, split in enumerate(("morton", "morton", "contiguous")):
+            i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, big_q.to(dev), 32,
+                                                  num_points=big_p.shape[0], dim=3, device=dev, split=split,
+                                                  out=peer)
+            out[f"peer{rep}"] = (i.cpu().clone(), d.cpu().clone())
+        peer.close()
         i, d = tdist.knn_sharded_batched(bp.to(dev), bq.to(dev), 8)
         out["batched"] = (i.cpu(), d.cpu())
         i, d = tdist.knn_sharded_ragged(rp.to(dev), bo, rq.to(dev), qo, 16)
@@ -113,6 +122,8 @@ def test_sharded_knn_on_two_gpus_matches_one_gpu():
         assert torch.equal(got["single_contiguous"][1], sd.cpu())
         i, d, rows = got["single_none"]
         assert torch.equal(i, si.cpu()[rows]) and torch.equal(d, sd.cpu()[rows])
+        for rep in range(3):
+            assert torch.equal(got[f"peer{rep}"][0], si.cpu()) and torch.equal(got[f"peer{rep}"][1], sd.cpu())
         assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
         assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())
     shares = [torch.load(Path(outdir) / f"rank{r}.pt")["single_none"][2] for r in range(2)]

@@ -1,0 +1,72 @@
+"""tbvh_query_knn_share on one GPU: a share of the queries of one cloud, each
+result row written at the query's own row of every destination buffer.
+
+On one GPU the destinations are local buffers; the multi-GPU form (peer-mapped
+destinations) is covered by tests/test_gpu_distributed.py.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import torchbvh_b200 as torchbvh
+from torchbvh_b200 import _native
+from torchbvh_b200._native import _C
+
+pytestmark = pytest.mark.gpu
+
+
+def _cloud(seed, shape):
+    g = torch.Generator().manual_seed(seed)
+    return torch.rand(shape, generator=g).cuda()
+
+
+@pytest.mark.parametrize("dim", [2, 3])
+@pytest.mark.parametrize("k", [4, 8, 16, 32])
+def test_shares_fill_their_rows_of_every_destination(dim, k):
+    points = _cloud(300 + dim + k, (5000, dim))
+    queries = _cloud(301 + dim + k, (2999, dim))
+    with torchbvh.BVH(points) as bvh:
+        h = bvh._handle
+        ref_idx, ref_dist = bvh.knn(queries, k)
+        order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                              h["scene_max"].unsqueeze(0))[0]
+        dests = [(torch.full((2999, k), -7, dtype=torch.int64, device="cuda"),
+                  torch.full((2999, k), -7.0, device="cuda")) for _ in range(2)]
+        cuts = [0, 1000, 2100, 2999]
+        for a, b in zip(cuts, cuts[1:]):
+            _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 5000, queries, order[a:b].contiguous(), k,
+                                    [d[0].data_ptr() for d in dests], [d[1].data_ptr() for d in dests])
+            torch.cuda.synchronize()
+            rows = order[b:]  # not served yet: untouched
+            for di, dd in dests:
+                assert bool((di[rows] == -7).all()) and bool((dd[rows] == -7.0).all())
+    for di, dd in dests:
+        assert torch.equal(di, ref_idx) and torch.equal(dd, ref_dist)
+    assert torchbvh.device_status() == 0
+
+
+def test_share_in_given_order_matches_too():
+    points = _cloud(7, (4096, 3))
+    queries = _cloud(8, (1500, 3))
+    with torchbvh.BVH(points) as bvh:
+        h = bvh._handle
+        ref_idx, ref_dist = bvh.knn(queries, 16)
+        di = torch.empty((1500, 16), dtype=torch.int64, device="cuda")
+        dd = torch.empty((1500, 16), device="cuda")
+        share = torch.arange(1500, dtype=torch.int64, device="cuda")
+        _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 4096, queries, share, 16,
+                                [di.data_ptr()], [dd.data_ptr()])
+    assert torch.equal(di, ref_idx) and torch.equal(dd, ref_dist)
+
+
+def test_peer_buffer_round_trip_on_one_device():
+    ptr, handle = _native.peer_alloc(0, 1024 * 8)
+    try:
+        t = _native.device_tensor(ptr, (1024,), torch.int64, torch.device("cuda", 0))
+        t.copy_(torch.arange(1024, device="cuda"))
+        torch.cuda.synchronize()
+        assert len(handle) == 64
+        assert int(t.sum()) == 1023 * 1024 // 2
+    finally:
+        _native.peer_free(0, ptr)

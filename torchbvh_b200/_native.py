@@ -56,6 +56,16 @@ _SIGNATURES = {
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),
+    "tbvh_peer_handle_bytes": (_size, []),
+    "tbvh_peer_alloc": (_i32, [_i32, _size, ctypes.POINTER(_ptr), _ptr]),
+    "tbvh_peer_free": (_i32, [_i32, _ptr]),
+    "tbvh_peer_open": (_i32, [_i32, _ptr, ctypes.POINTER(_ptr)]),
+    "tbvh_peer_close": (_i32, [_i32, _ptr]),
+    "tbvh_query_knn_share": (
+        _i32,
+        [_i32, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i32, _i32, _i32, ctypes.POINTER(_ptr),
+         ctypes.POINTER(_ptr), _ptr],
+    ),
     "tbvh_query_knn_gather": (
         _i32,
         [_i32, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i32, _i32, _ptr, _ptr, _ptr, _ptr,
@@ -417,6 +427,82 @@ def query_knn_ragged(packed: dict, query_points: torch.Tensor, query_offsets: to
         for h in hooks:
             h("end", device)
     return (indices, distances) if positions is None else (indices, distances, positions)
+
+
+# ---------------------------------------------------------------------------
+# Peer-delivered results (one cloud sharded over the GPUs of a node)
+# ---------------------------------------------------------------------------
+
+def peer_alloc(device: int, nbytes: int) -> tuple[int, bytes]:
+    """IPC-shareable device buffer: (pointer, handle bytes for the other processes)."""
+    lib = load_library()
+    handle = ctypes.create_string_buffer(int(lib.tbvh_peer_handle_bytes()))
+    ptr = _ptr()
+    _check(lib.tbvh_peer_alloc(int(device), int(nbytes), ctypes.byref(ptr), ctypes.cast(handle, _ptr)))
+    return int(ptr.value), handle.raw
+
+
+def peer_open(device: int, handle: bytes) -> int:
+    """Maps another process's buffer (from peer_alloc) on `device`; returns its address there."""
+    lib = load_library()
+    buf = ctypes.create_string_buffer(handle, len(handle))
+    ptr = _ptr()
+    _check(lib.tbvh_peer_open(int(device), ctypes.cast(buf, _ptr), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_close(device: int, ptr: int) -> None:
+    _check(load_library().tbvh_peer_close(int(device), _ptr(ptr)))
+
+
+def peer_free(device: int, ptr: int) -> None:
+    _check(load_library().tbvh_peer_free(int(device), _ptr(ptr)))
+
+
+class _DeviceView:
+    """__cuda_array_interface__ of a raw device buffer, for a zero-copy tensor view."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+def device_tensor(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """Tensor over memory this module owns (no copy; the owner must outlive it)."""
+    typestr = {torch.int64: "<i8", torch.float32: "<f4"}[dtype]
+    with torch.cuda.device(device):
+        return torch.as_tensor(_DeviceView(ptr, shape, typestr), device=device)
+
+
+def query_knn_share(node_aabbs: torch.Tensor, sorted_indices: torch.Tensor, num_points: int,
+                    queries: torch.Tensor, share: torch.Tensor, k: int,
+                    dest_indices: list[int], dest_distances: list[int]) -> None:
+    """k-NN of the queries listed in `share` (int64 indices into `queries`), each result
+    row written at the query's row of every destination buffer (tbvh_query_knn_share)."""
+    op = "query_knn_share"
+    if not (queries.is_cuda and queries.is_contiguous() and queries.dtype == torch.float32 and queries.dim() == 2):
+        raise RuntimeError(f"{op}: queries must be contiguous CUDA float32 (M, D)")
+    if not (share.is_cuda and share.is_contiguous() and share.dtype == torch.int64 and share.dim() == 1):
+        raise RuntimeError(f"{op}: share must be contiguous CUDA int64 (count,)")
+    if len(dest_indices) != len(dest_distances) or not dest_indices:
+        raise RuntimeError(f"{op}: one distance buffer per index buffer")
+    device = queries.device
+    lib = load_library()
+    n_dest = len(dest_indices)
+    idx_arr = (_ptr * n_dest)(*[_ptr(p) for p in dest_indices])
+    dist_arr = (_ptr * n_dest)(*[_ptr(p) for p in dest_distances])
+    hooks = _knn_hooks
+    if hooks:
+        for h in hooks:
+            h("start", device)
+    _check(lib.tbvh_query_knn_share(
+        device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), int(num_points), queries.data_ptr(),
+        int(queries.size(0)), share.data_ptr(), int(share.numel()), int(queries.size(1)), int(k), n_dest,
+        idx_arr, dist_arr, _stream(device),
+    ))
+    if hooks:
+        for h in hooks:
+            h("end", device)
 
 
 # Optional observers of the traversal launch (bench.py times the kernel with

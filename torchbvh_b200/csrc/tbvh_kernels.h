@@ -12,7 +12,10 @@ namespace tbvh {
 
 // ---- radix sort (stable LSD, 8-bit digits, decoupled look-back) -----------
 constexpr int kSortThreads = 256;
-constexpr int kSortIpt = 16;
+#ifndef TBVH_SORT_IPT
+#define TBVH_SORT_IPT 16
+#endif
+constexpr int kSortIpt = TBVH_SORT_IPT;  // keys per thread in one sort tile
 constexpr int kSortTile = kSortThreads * kSortIpt;  // elements per tile
 constexpr int kRadix = 256;
 constexpr int kMaxSortPasses = 8;
@@ -94,6 +97,7 @@ struct QuerySortLaunch {
 cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream);
 
 // ---- k-NN traversal ----------------------------------------------------------
+constexpr int kMaxDest = 8;  // result destinations of one k-NN launch (GPUs of one node)
 struct KnnLaunch {
   const float* node_aabbs;
   const int64_t* sorted_indices;
@@ -113,6 +117,12 @@ struct KnnLaunch {
   const float* source_points = nullptr;  // fused neighbour-position gather (nullable)
   float* out_positions = nullptr;
   bool spatial = false;                  // output rows in sorted order
+  // Result rows delivered to every destination (row = query index), instead of
+  // out_idx/out_dist, when num_dest > 0. Destinations may be peer-mapped
+  // buffers of other GPUs (NVLink stores).
+  int num_dest = 0;
+  int64_t* dest_idx[kMaxDest] = {};
+  float* dest_dist[kMaxDest] = {};
 };
 
 cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream);

@@ -61,6 +61,9 @@ struct KnnArgs {
   const float* src_points;  // nullable: fused neighbour-position gather source
   float* out_pos;           // nullable: (rows, K, D) neighbour positions
   int spatial;              // 1: write row = sorted (Morton) position, else the query's own row
+  int num_dest;             // > 0: rows go to dest_* (row = query index) instead of out_*
+  int64_t* dest_idx[kMaxDest];
+  float* dest_dist[kMaxDest];
   unsigned* status;
 };
 
@@ -143,7 +146,7 @@ __device__ __forceinline__ void load_leaf(const float* rows, int64_t row, float*
   if constexpr (D == 3) p[2] = __ldg(r + 2);
 }
 
-template <int D, int K>
+template <int D, int K, bool kToDest>
 __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int cloud, bool mine, int64_t pos,
                                              unsigned lane, unsigned warp) {
   // Cloud facts.
@@ -373,7 +376,25 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   }
   (void)nd;
 
-  if (mine) {
+  if constexpr (kToDest) {
+    if (!mine) return;
+    // Result row delivered to every destination buffer at the query's row.
+    // Destinations on other GPUs are written over NVLink as the results come
+    // out of the traversal, so the exchange overlaps the remaining compute.
+    for (int dst = 0; dst < a.num_dest; ++dst) {
+      int64_t* oi = a.dest_idx[dst] + gq * K;
+      float* od = a.dest_dist[dst] + gq * K;
+#pragma unroll
+      for (int i = 0; i < K; i += 2) {
+        reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(key[i]), key_idx(key[i + 1]));
+      }
+#pragma unroll
+      for (int i = 0; i < K; i += 4) {
+        reinterpret_cast<float4*>(od)[i / 4] =
+            make_float4(key_dist(key[i]), key_dist(key[i + 1]), key_dist(key[i + 2]), key_dist(key[i + 3]));
+      }
+    }
+  } else if (mine) {
     // Output row: the query's own row, or its position in the sorted order
     // (the reference's spatial variant, knn_query.cu:448-461).
     const int64_t row = a.spatial ? pos : gq;
@@ -404,7 +425,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   }
 }
 
-template <int D, int K>
+template <int D, int K, bool kToDest>
 __global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
   extern __shared__ __align__(16) unsigned char knn_smem_raw[];
   KnnSmem& s = *reinterpret_cast<KnnSmem*>(knn_smem_raw);
@@ -419,8 +440,11 @@ __global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
     const int cur = __shfl_sync(kFullMask, cloud, leader);
     const bool mine = valid && cloud == cur;
     pending &= ~__ballot_sync(kFullMask, mine);
-    search_cloud<D, K>(a, s, cur, mine, pos, lane, warp);
+    search_cloud<D, K, kToDest>(a, s, cur, mine, pos, lane, warp);
   }
+  // Peer stores must be visible system-wide before the kernel counts as done:
+  // the caller's next collective tells the other GPUs that their rows arrived.
+  if constexpr (kToDest) __threadfence_system();
 }
 
 // Per-cloud table for ragged queries (n, leaf level, first node row).
@@ -465,7 +489,11 @@ cudaError_t launch_typed(const KnnArgs& a, cudaStream_t stream) {
   const int64_t blocks = (warps + kKnnWarps - 1) / kKnnWarps;
   if (blocks > 0) {
     static_assert(sizeof(KnnSmem) <= 48 * 1024, "fits the default dynamic shared memory limit");
-    k_knn<D, K><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
+    if (a.num_dest > 0) {
+      k_knn<D, K, true><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
+    } else {
+      k_knn<D, K, false><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
+    }
     count_launches(1);
   }
   return cudaGetLastError();
@@ -489,6 +517,11 @@ cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream) {
   a.src_points = q.source_points;
   a.out_pos = q.out_positions;
   a.spatial = q.spatial ? 1 : 0;
+  a.num_dest = q.num_dest;
+  for (int i = 0; i < kMaxDest; ++i) {
+    a.dest_idx[i] = q.dest_idx[i];
+    a.dest_dist[i] = q.dest_dist[i];
+  }
   a.status = device_status_ptr();
   if (q.points.uniform_n > 0) {
     a.table = nullptr;

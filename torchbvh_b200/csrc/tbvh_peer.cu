@@ -1,0 +1,152 @@
+// Peer-delivered k-NN results for one cloud sharded over the GPUs of a node.
+//
+// The reference is single-GPU and gathers nothing. Its sharded counterpart
+// here (torchbvh_b200.distributed.knn_sharded_single_cloud) gives every rank a
+// share of the queries; with an all-gathered result every rank needs every
+// row. Instead of a collective after the traversal, tbvh_query_knn_share has
+// the traversal write each finished row straight into every rank's (M, k)
+// output at the query's own row: local rows to HBM, remote rows as NVLink
+// stores into buffers mapped with CUDA IPC. The exchange then overlaps the
+// rest of the traversal. No kernel waits on another GPU; ordering across ranks
+// comes from the caller's collectives (see the header).
+//
+// The buffers are plain cudaMalloc allocations shared through
+// cudaIpcGetMemHandle / cudaIpcOpenMemHandle: point-to-point mappings only,
+// nothing is bound to an NVLink multicast object.
+#include <climits>
+#include <cstdio>
+
+#include "../../include/torchbvh_b200.h"
+#include "tbvh_kernels.h"
+
+namespace {
+
+int peer_fail(int code, const char* op, const char* what) {
+  char buf[384];
+  snprintf(buf, sizeof(buf), "%s: %s", op, what);
+  return tbvh::record_error(code, buf);
+}
+
+int peer_cuda_fail(cudaError_t e, const char* op) {
+  char buf[384];
+  snprintf(buf, sizeof(buf), "%s: CUDA error %s (%s)", op, cudaGetErrorName(e), cudaGetErrorString(e));
+  return tbvh::record_error(TBVH_ERR_CUDA, buf);
+}
+
+int peer_set_device(int device, const char* op) {
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur == device) return TBVH_OK;
+  const cudaError_t e = cudaSetDevice(device);
+  return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tbvh_peer_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int tbvh_peer_alloc(int device, size_t bytes, void** out_ptr, void* out_handle) {
+  const char* op = "tbvh_peer_alloc";
+  tbvh::record_error(TBVH_OK, "");
+  if (!out_ptr || !out_handle || bytes == 0) return peer_fail(TBVH_ERR_BAD_ARG, op, "bad arguments");
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return peer_cuda_fail(e, op);
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return peer_cuda_fail(e, op);
+  }
+  *out_ptr = p;
+  *static_cast<cudaIpcMemHandle_t*>(out_handle) = h;
+  return TBVH_OK;
+}
+
+int tbvh_peer_free(int device, void* ptr) {
+  const char* op = "tbvh_peer_free";
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
+}
+
+int tbvh_peer_open(int device, const void* handle, void** out_ptr) {
+  const char* op = "tbvh_peer_open";
+  tbvh::record_error(TBVH_OK, "");
+  if (!handle || !out_ptr) return peer_fail(TBVH_ERR_BAD_ARG, op, "bad arguments");
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  void* p = nullptr;
+  const cudaError_t e =
+      cudaIpcOpenMemHandle(&p, *static_cast<const cudaIpcMemHandle_t*>(handle), cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return peer_cuda_fail(e, op);
+  *out_ptr = p;
+  return TBVH_OK;
+}
+
+int tbvh_peer_close(int device, void* ptr) {
+  const char* op = "tbvh_peer_close";
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
+}
+
+int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
+                         const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
+                         int dim, int k, int num_dest, int64_t* const* dest_indices,
+                         float* const* dest_distances, void* stream) {
+  const char* op = "query_knn_share";
+  tbvh::record_error(TBVH_OK, "");
+  if (dim != 2 && dim != 3) return peer_fail(TBVH_ERR_BAD_ARG, op, "D must be 2 or 3");
+  if (k != 4 && k != 8 && k != 16 && k != 32)
+    return peer_fail(TBVH_ERR_UNSUPPORTED_K, op, "k must be 4, 8, or 16 (or 32)");
+  if (num_points < 1 || num_points > INT_MAX)
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "point count must be in [1, 2^31)");
+  if (num_points < k) return peer_fail(TBVH_ERR_BAD_ARG, op, "num_leaves must be >= k");
+  if (num_queries < 0 || num_queries > INT_MAX)
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "query count must fit in signed int32");
+  if (share_count < 0 || share_count > num_queries)
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "share_count must be in [0, num_queries]");
+  if (num_dest < 1 || num_dest > tbvh::kMaxDest)
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "num_dest must be in [1, 8]");
+  if (!dest_indices || !dest_distances) return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL destination list");
+  for (int i = 0; i < num_dest; ++i)
+    if (!dest_indices[i] || !dest_distances[i]) return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL destination buffer");
+  if (share_count == 0) return TBVH_OK;
+  if (!node_aabbs || !sorted_indices || !queries || !order)
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL input pointer");
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  tbvh::KnnLaunch q{};
+  q.node_aabbs = node_aabbs;
+  q.sorted_indices = sorted_indices;
+  q.queries = queries;
+  q.order = order;
+  q.points.offsets = nullptr;
+  q.points.uniform_n = num_points;
+  q.points.num_clouds = 1;
+  // One cloud of num_queries queries, of which this launch serves the
+  // share_count positions listed in `order`.
+  q.queries_map.offsets = nullptr;
+  q.queries_map.uniform_n = num_queries;
+  q.queries_map.num_clouds = 1;
+  q.uniform = tbvh::cloud_tree_facts(num_points);
+  q.uniform_rows = tbvh::real_node_count(num_points);
+  q.total_queries = share_count;
+  q.dim = dim;
+  q.k = k;
+  q.num_dest = num_dest;
+  for (int i = 0; i < num_dest; ++i) {
+    q.dest_idx[i] = dest_indices[i];
+    q.dest_dist[i] = dest_distances[i];
+  }
+  const cudaError_t e = tbvh::launch_knn(q, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
+}
+
+}  // extern "C"

@@ -95,10 +95,102 @@ def _morton_share_cuda(points: torch.Tensor, queries: torch.Tensor, k: int, q0: 
     return order, mine, idx, dist_sq
 
 
+class PeerResults:
+    """(M, k) result buffers on every rank of `group`, each mapped on every other
+    rank through CUDA IPC, for ``knn_sharded_single_cloud(..., gather="all", out=...)``.
+
+    With it, the all-gather is fused into the traversal: each rank writes every
+    result row of its share into all ranks' buffers (NVLink stores) as the rows
+    are produced, instead of an NCCL all-gather after the traversal.
+    ``indices`` / ``distances`` are this rank's (M, k) buffers; a call
+    overwrites them, so read (or copy) the results before the next call with
+    the same object. Create once, reuse across calls, ``close()`` on every
+    rank together (a collective).
+    """
+
+    def __init__(self, num_queries: int, k: int, *, group=None, device: torch.device | None = None):
+        from . import _native
+
+        self.group = group
+        self.world, self.rank = _world(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.num_queries, self.k = int(num_queries), int(k)
+        dev = self.device.index
+        rows = max(self.num_queries, 1) * self.k
+        self._own = [_native.peer_alloc(dev, rows * 8), _native.peer_alloc(dev, rows * 4)]
+        handles = [None] * self.world
+        dist.all_gather_object(handles, (self._own[0][1], self._own[1][1]), group=group)
+        self._opened: list[int] = []
+        self.dest_indices: list[int] = []
+        self.dest_distances: list[int] = []
+        for r in range(self.world):
+            if r == self.rank:
+                pi, pd = self._own[0][0], self._own[1][0]
+            else:
+                pi = _native.peer_open(dev, handles[r][0])
+                pd = _native.peer_open(dev, handles[r][1])
+                self._opened += [pi, pd]
+            self.dest_indices.append(pi)
+            self.dest_distances.append(pd)
+        shape = (self.num_queries, self.k)
+        self.indices = _native.device_tensor(self._own[0][0], shape, torch.int64, self.device)
+        self.distances = _native.device_tensor(self._own[1][0], shape, torch.float32, self.device)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.closed = False
+
+    def delivered(self) -> None:
+        """Collective on the current stream after the writing launches: once it
+        completes on a rank, every peer's rows have arrived in its buffers."""
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self) -> None:
+        from . import _native
+
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._opened:
+            _native.peer_close(self.device.index, p)
+        dist.barrier(group=self.group)
+        for p, _ in self._own:
+            _native.peer_free(self.device.index, p)
+        self.indices = self.distances = None
+        self.closed = True
+
+    def __enter__(self) -> "PeerResults":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+
+def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, q0: int, q1: int, split: str,
+                    out: PeerResults):
+    """One BVH build; this rank's share of the queries (a range of their Morton
+    order, or of their given order); results delivered to every rank's `out`."""
+    from ._bvh_class import BVH
+    from ._native import _C, query_knn_share
+
+    with BVH(points) as bvh:
+        h = bvh._handle
+        if split == "morton":
+            order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                                  h["scene_max"].unsqueeze(0))[0]
+            share = order[q0:q1]
+        else:
+            share = torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
+        query_knn_share(h["node_aabbs"], h["sorted_indices"], points.shape[0], queries, share, k,
+                        out.dest_indices, out.dest_distances)
+    out.delivered()
+    return out.indices, out.distances
+
+
 def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor, k: int, *,
                              num_points: int, dim: int, src: int = 0, group=None, gather: str = "all",
                              split: str = "morton", order_fn: Callable | None = None,
-                             knn_fn: KnnFn = default_knn, device: torch.device | None = None):
+                             knn_fn: KnnFn = default_knn, device: torch.device | None = None,
+                             out: "PeerResults | None" = None):
     """Exact k-NN of one cloud with the queries split over ranks.
 
     `points` is read on rank `src` only (other ranks may pass None); every rank
@@ -110,6 +202,10 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     "root" only on `src` (None elsewhere), "none" returns this rank's rows and
     which queries they belong to (the (start, end) range for "contiguous", the
     int64 query indices for "morton").
+
+    `out` (a PeerResults, gather="all" with the CUDA path only): the traversal
+    itself delivers every row to every rank; the returned tensors are views of
+    `out`, valid until the next call with it.
     """
     if split not in ("morton", "contiguous"):
         raise ValueError("knn_sharded_single_cloud: split must be 'morton' or 'contiguous'")
@@ -120,6 +216,12 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     dist.broadcast(buf, src=src, group=group)
     m = queries.shape[0]
     q0, q1 = shard_range(m, world, rank)
+    if out is not None:
+        if gather != "all" or knn_fn is not default_knn or order_fn is not None:
+            raise ValueError("knn_sharded_single_cloud: out= needs gather='all' and the CUDA path")
+        if out.num_queries != m or out.k != k:
+            raise ValueError("knn_sharded_single_cloud: out= was made for another query count or k")
+        return _share_to_peers(buf, queries.contiguous(), k, q0, q1, split, out)
     order = None
     if split == "contiguous":
         idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
