@@ -155,7 +155,8 @@ int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* so
  * step of the broadcast + split + all-gather form of one large cloud.
  *
  * Buffers that other GPUs write into are shared with CUDA IPC:
- * tbvh_peer_alloc allocates `bytes` on `device` (cudaMalloc) and fills
+ * tbvh_peer_alloc allocates `bytes` (rounded up to whole 2 MiB, so that the
+ * buffer is an allocation of its own) on `device` (cudaMalloc) and fills
  * out_handle (tbvh_peer_handle_bytes() bytes) for the other processes;
  * tbvh_peer_open maps such a handle on `device` (point-to-point mapping, no
  * multicast); tbvh_peer_close / tbvh_peer_free undo them. Synchronous.

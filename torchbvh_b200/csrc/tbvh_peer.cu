@@ -52,6 +52,11 @@ int tbvh_peer_alloc(int device, size_t bytes, void** out_ptr, void* out_handle) 
   if (!out_ptr || !out_handle || bytes == 0) return peer_fail(TBVH_ERR_BAD_ARG, op, "bad arguments");
   int rc = peer_set_device(device, op);
   if (rc) return rc;
+  // Whole 2 MiB units: a small request may be placed inside a larger block
+  // that the driver shares between allocations, and an IPC handle maps the
+  // block from its start, so another process would not see this pointer.
+  constexpr size_t kUnit = size_t(2) << 20;
+  bytes = (bytes + kUnit - 1) / kUnit * kUnit;
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) return peer_cuda_fail(e, op);
