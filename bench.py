@@ -393,9 +393,10 @@ def run_b200(args, world, rank, local):
         "launches": len(knn_ms),
     }
 
-    cpu = None
+    cpu = cpu_bf = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w, args)
+        cpu_bf = cpu_bruteforce_throughput(w)
 
     result = {
         "metric": METRIC,
@@ -418,6 +419,7 @@ def run_b200(args, world, rank, local):
         "build_algorithmic_bytes": build_bytes,
         "roofline": roofline,
         "cpu_baseline": cpu,
+        "cpu_bruteforce": cpu_bf,
         "e2e": e2e,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
@@ -657,6 +659,61 @@ def cpu_port_throughput(w, args, budget_s: float = 12.0) -> dict:
 
 def cpu_baseline(w, args) -> dict:
     return cpu_port_throughput(w, args)
+
+
+def cpu_bruteforce_throughput(w, budget_s: float = 8.0, chunk_bytes: int = 1 << 28) -> dict:
+    """CPU brute force the north star asks to report beside the GPU numbers:
+    ``torch.cdist(q, p).topk(k, largest=False)`` (default compute mode) plus the
+    square, on all host threads, over a bounded sample: queries of the first
+    clouds, in chunks whose distance matrix stays near `chunk_bytes`, until
+    about `budget_s` seconds are spent. Brute force costs the same per query
+    within a cloud, so per-cloud query rates extrapolate to the whole workload.
+    """
+    threads = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        sizes, pts, qs = _cpu_sample(w, 0)
+        qcounts = ([int(q.shape[0]) for q in qs])
+        est_s = 0.0
+        sampled = 0
+        spent = 0.0
+        clouds_used = 0
+        per_query_s = []
+        for b in range(len(sizes)):
+            p = pts[b].contiguous()
+            q_all = qs[b]
+            rows = max(1, min(int(q_all.shape[0]), chunk_bytes // max(1, 4 * int(p.shape[0]))))
+            done = 0
+            t_cloud = 0.0
+            while done < q_all.shape[0] and (t_cloud < budget_s / 4 or done == 0):
+                q = q_all[done:done + rows].contiguous()
+                t0 = time.perf_counter()
+                d, i = torch.cdist(q, p).topk(w.k, dim=1, largest=False)
+                d = d.square()
+                t_cloud += time.perf_counter() - t0
+                done += q.shape[0]
+            per_query_s.append(t_cloud / done)
+            sampled += done
+            spent += t_cloud
+            clouds_used += 1
+            if spent > budget_s:
+                break
+        # Clouds not sampled cost like the sampled one closest in size (cost ~ N per query).
+        for b in range(len(sizes)):
+            j = min(range(len(per_query_s)), key=lambda c: abs(sizes[c] - sizes[b]))
+            est_s += per_query_s[j] * (sizes[b] / sizes[j]) * qcounts[b]
+        return {
+            "value": w.num_queries / est_s,
+            "unit": UNIT,
+            "cores": threads,
+            "kind": "torch.cdist + topk brute force",
+            "sample": (f"{sampled} queries of {clouds_used} of {len(sizes)} clouds, chunks of up to "
+                       f"{chunk_bytes >> 20} MiB of distances; per-query time scaled by cloud size to the "
+                       f"whole workload"),
+        }
+    finally:
+        torch.set_num_threads(prev)
 
 
 def run_reference(args, world, rank):
