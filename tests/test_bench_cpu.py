@@ -40,3 +40,9 @@ def test_workload_config_names_the_workload(bench):
     cfg = bench.workload_config(w, 1)
     assert cfg["workload"].startswith("c1") and cfg["k"] == 4 and cfg["parallelism"] == "single GPU"
     assert "dp8" in bench.workload_config(w, 8)["parallelism"]
+
+
+def test_bruteforce_baseline_covers_batched_clouds(bench):
+    w = workloads.make("c2", batch=3, n=2048)
+    out = bench.cpu_bruteforce_throughput(w, budget_s=0.2)
+    assert out["value"] > 0 and "of 3 clouds" in out["sample"]
