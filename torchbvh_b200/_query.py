@@ -25,7 +25,7 @@ from ._handles import (
     _bvh_data,
     _ragged_bvh_data,
 )
-from ._native import _C, real_node_count
+from ._native import _C
 from ._validation import (
     _as_contiguous,
     _as_contiguous_int64,
