@@ -151,3 +151,21 @@ def test_gather_neighbor_values_shape_checks_on_cpu():
         torchbvh.gather_neighbor_values(values, torch.zeros((2, 6, 2, 2), dtype=torch.int64))
     with pytest.raises(ValueError, match="values must be a CUDA tensor"):
         torchbvh.gather_neighbor_values(values, torch.zeros((2, 6, 3, 2), dtype=torch.int64))
+
+
+def test_package_surface_matches_the_reference_knn_exports():
+    # torchbvh/__init__.py exports BVH but no BatchedBVH / RaggedBVH classes, and its
+    # k-NN workflows and constants by these names.
+    assert hasattr(torchbvh, "BVH") and "BVH" in torchbvh.__all__
+    for absent in ("BatchedBVH", "RaggedBVH"):
+        assert not hasattr(torchbvh, absent) and absent not in torchbvh.__all__
+    for name in ("BVHHandle", "BatchedBVHHandle", "RaggedBVHHandle", "build_bvh", "destroy_bvh", "query_knn",
+                 "query_displaced_knn", "gather_neighbor_values", "interpolate_displaced", "SUPPORTED_K",
+                 "SUPPORTED_DIMS"):
+        assert name in torchbvh.__all__ and hasattr(torchbvh, name)
+
+
+def test_bvh_class_is_not_a_mapping():
+    assert not hasattr(torchbvh.BVH, "__getitem__")
+    for method in ("knn", "destroy", "__enter__", "__exit__"):
+        assert callable(getattr(torchbvh.BVH, method))
