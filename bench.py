@@ -11,7 +11,10 @@ points, k = 16). Metric: k-NN queries/sec (build + query).
 * ``value``: device-resident inputs, CUDA events around each step on the
   current stream, L2 flushed (256 MiB write) between steps outside the events,
   summed over K steps, max over ranks. Under torchrun every rank runs the
-  workload on its own GPU with no data exchange (weak scaling).
+  workload on its own GPU with no data exchange (weak scaling), except c4:
+  one cloud, its points broadcast from rank 0, queries split by Morton range,
+  results left on the computing rank (strong scaling), with an ``all_gather``
+  figure where the traversal delivers every row to every GPU over NVLink.
 * ``e2e``: the same public API with the inputs in pinned host memory: per step
   H2D copy of points and queries, build, query, D2H copy of indices and
   distances, all inside the events.
@@ -19,6 +22,8 @@ points, k = 16). Metric: k-NN queries/sec (build + query).
   launch over its event-timed duration, against MEASURED_PEAKS.json hbm_gbs.
 * ``cpu_baseline``: the CPU port of the reference algorithm (oracle/, C,
   all host threads) on a bounded sample of the same workload, rank 0 only.
+* ``cpu_bruteforce``: ``torch.cdist`` + ``topk`` on all host threads over a
+  bounded sample, extrapolated (rank 0, one GPU only).
 * ``--impl reference``: that CPU port as the reference arm (the reference's k-NN
   has no CPU implementation of its own). ``--impl reference_cuda``: the
   reference's CUDA path from baseline/_ref, if installed.
