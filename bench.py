@@ -5,16 +5,21 @@
 
 A step is one ``BVH(points)`` build plus one ``.knn(queries, k)`` query over one
 batch of the seeded synthetic workload (torchbvh_b200.workloads), through the
-public API. Default workload: c2 (16 Gaussian-mixture clouds x 65,536 3-D
-points, k = 16). Metric: k-NN queries/sec (build + query).
+public API. Default workload: c4, the largest configuration and the only one
+that is strong-scaled (one sphere-shell cloud of 16,777,216 3-D points, as many
+queries, k = 32). Metric: k-NN queries/sec (build + query).
 
 * ``value``: device-resident inputs, CUDA events around each step on the
   current stream, L2 flushed (256 MiB write) between steps outside the events,
-  summed over K steps, max over ranks. Under torchrun every rank runs the
-  workload on its own GPU with no data exchange (weak scaling), except c4:
-  one cloud, its points broadcast from rank 0, queries split by Morton range,
-  results left on the computing rank (strong scaling), with an ``all_gather``
-  figure where the traversal delivers every row to every GPU over NVLink.
+  summed over K steps, max over ranks. On one GPU: build + query. On N > 1
+  GPUs, c4 is one cloud sharded over the ranks (strong scaling): rank 0's
+  points broadcast, the BVH built on every rank, the queries split by Morton
+  range, and every result row delivered to every rank (the traversal writes
+  each row into all ranks' buffers over NVLink), i.e. results all-gathered;
+  ``results_in_place`` times the same step with the rows left on the rank
+  that computed them, ``nccl_all_gather`` with an NCCL all-gather after the
+  traversal instead. The other workloads on N GPUs run N replicas (weak
+  scaling).
 * ``e2e``: the same public API with the inputs in pinned host memory: per step
   H2D copy of points and queries, build, query, D2H copy of indices and
   distances, all inside the events.
@@ -56,7 +61,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c4", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -65,8 +70,6 @@ def parse_args():
     ap.add_argument("--c4-split", default="morton", choices=["morton", "contiguous"],
                     help="c4 on N > 1 GPUs: share of the queries per rank (a range of their Morton order, "
                          "or of their given order)")
-    ap.add_argument("--cpu-sample-queries", type=int, default=0,
-                    help="queries per sampled cloud for the CPU baseline (0 = automatic)")
     return ap.parse_args()
 
 
@@ -488,25 +491,26 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         return sum(a.elapsed_time(b) for a, b in ev), launches
 
     resident = lambda: (points, queries)  # noqa: E731
-    _native._knn_hooks.append(hook)
-    sampler = ClockSampler(local)
-    with sampler:
-        total_ms, launches = timed("none", args.steps, args.warmup, resident)
-    _native._knn_hooks.remove(hook)
-    total_ms_max = max_over_ranks(total_ms, world)
-    starts = [e for ph, e in knn_events if ph == "start"][-args.steps:]
-    ends = [e for ph, e in knn_events if ph == "end"][-args.steps:]
-    knn_local_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / len(starts)
-    knn_avg_ms = max_over_ranks(knn_local_ms, world)
-    import torch.distributed as dist
-
-    per_rank = [None] * world
-    dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps})
-
+    # value: results all-gathered, the traversal delivering every row to every
+    # rank's buffer over NVLink (PeerResults, reused across steps).
     gather_steps = max(3, min(args.steps, 10))
-    nccl_gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
     with tdist.PeerResults(m, k, device=device) as peer:
-        gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident, peer)[0], world)
+        _native._knn_hooks.append(hook)
+        sampler = ClockSampler(local)
+        with sampler:
+            total_ms, launches = timed("all", args.steps, args.warmup, resident, peer)
+        _native._knn_hooks.remove(hook)
+        total_ms_max = max_over_ranks(total_ms, world)
+        starts = [e for ph, e in knn_events if ph == "start"][-args.steps:]
+        ends = [e for ph, e in knn_events if ph == "end"][-args.steps:]
+        knn_local_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / len(starts)
+        knn_avg_ms = max_over_ranks(knn_local_ms, world)
+        import torch.distributed as dist
+
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps})
+    inplace_ms = max_over_ranks(timed("none", gather_steps, 3, resident)[0], world)
+    nccl_gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
     status = torchbvh.device_status(device)
 
     e2e = None
@@ -568,13 +572,14 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         "config": {**workload_config(w, world),
                    "parallelism": (f"points broadcast from rank 0 (NCCL), BVH built on each of {world} GPUs, "
                                    f"queries split by {'Morton-order' if args.c4_split == 'morton' else 'index'} "
-                                   f"range, results left on the computing rank")},
-        "all_gather": {"value": m * gather_steps / (gather_ms / 1e3), "unit": UNIT,
-                       "ms_per_step": gather_ms / gather_steps,
-                       "note": ("same step with every (M, k) result row delivered to every rank in query order: "
-                                "the traversal writes each row into all ranks' buffers over NVLink as it "
-                                "finishes (tbvh_query_knn_share)"),
-                       "nccl_all_gather_ms_per_step": nccl_gather_ms / gather_steps},
+                                   f"range, every result row delivered to every rank by the traversal "
+                                   f"(NVLink stores): results all-gathered")},
+        "results_in_place": {"value": m * gather_steps / (inplace_ms / 1e3), "unit": UNIT,
+                             "ms_per_step": inplace_ms / gather_steps,
+                             "note": "same step with each result row left on the rank that computed it"},
+        "nccl_all_gather": {"value": m * gather_steps / (nccl_gather_ms / 1e3), "unit": UNIT,
+                            "ms_per_step": nccl_gather_ms / gather_steps,
+                            "note": "rows left in place by the traversal, then an NCCL all-gather into query order"},
         "knn_kernel_ms": knn_avg_ms,
         "per_rank_ms": per_rank,
         "roofline": {"kernel": "k_knn (warp-packet BVH traversal), one rank's share", "bound": "hbm",
@@ -595,8 +600,8 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
 # CPU port (oracle) timing: cpu_baseline and the reference arm
 # ---------------------------------------------------------------------------
 
-def _cpu_sample(w, sample_queries: int):
-    """Bounded sample: the first clouds (whole), a prefix of their queries."""
+def _cpu_sample(w):
+    """Per-cloud point and query arrays of a workload (CPU tensors)."""
     sizes = w.cloud_sizes()
     if w.points.dim() == 3:
         pts = [w.points[b] for b in range(w.points.shape[0])]
@@ -611,58 +616,92 @@ def _cpu_sample(w, sample_queries: int):
     return sizes, pts, qs
 
 
-def cpu_port_throughput(w, args, budget_s: float = 12.0) -> dict:
-    """Times the C port of the reference algorithm on host cores; extrapolates q/s.
+class CpuPortSample:
+    """The C port of the reference algorithm (oracle/, build + DFS traversal) over a
+    bounded sample of a workload, on the host cores.
 
-    Per sampled cloud: full build timed, then a prefix of its queries (the
-    per-query cost is independent of how many are run). Clouds are sampled
-    until about `budget_s` seconds of CPU work are spent.
+    Construction builds the first clouds in full, one thread each (the port's
+    build is serial), until about `build_budget_s` is spent; clouds are
+    independent, so a whole workload builds `min(threads, clouds)` clouds at a
+    time. Each `step(budget_s)` traverses fresh queries of those clouds (a
+    rolling window over each cloud's queries) on `threads` threads for about
+    `budget_s` seconds. A traversal costs the same per query whichever queries of
+    a cloud are drawn, so the measured rate scales to the whole workload:
+    estimated seconds = build s/point x points / min(threads, clouds)
+    + traversal s/query x queries.
     """
-    import numpy as np
 
-    from oracle import pyoracle
+    def __init__(self, w, build_budget_s: float = 4.0):
+        import numpy as np
 
-    threads = pyoracle.default_threads()
-    sizes, pts, qs = _cpu_sample(w, 0)
-    m_total = w.num_queries
-    per_cloud_q = args.cpu_sample_queries or (8192 if w.num_points <= 20_000_000 else 65536)
-    build_s = query_s = 0.0
-    built_points = sampled_queries = 0
-    clouds_used = 0
-    t_start = time.perf_counter()
-    order = sorted(range(len(sizes)), key=lambda b: b)  # deterministic: first clouds first
-    for b in order:
-        p = np.ascontiguousarray(pts[b].numpy())
-        q = np.ascontiguousarray(qs[b][:per_cloud_q].numpy())
-        po = np.array([0, p.shape[0]], np.int64)
-        qo = np.array([0, q.shape[0]], np.int64)
-        _, _, tb, tq = pyoracle.build_and_query(p, po, q, qo, w.k, threads)
-        build_s += tb
-        query_s += tq
-        built_points += p.shape[0]
-        sampled_queries += q.shape[0]
-        clouds_used += 1
-        if time.perf_counter() - t_start > budget_s:
-            break
-    build_per_point = build_s / built_points
-    query_per_query = query_s / sampled_queries
-    est_s = build_per_point * w.num_points + query_per_query * m_total
+        from oracle import pyoracle
+
+        self._np, self._oracle = np, pyoracle
+        self.w = w
+        self.threads = pyoracle.default_threads()
+        sizes, pts, qs = _cpu_sample(w)
+        self.total_clouds = len(sizes)
+        self.trees, self.queries = [], []
+        build_s = 0.0
+        self.built_points = 0
+        for b in range(len(sizes)):
+            p = np.ascontiguousarray(pts[b].numpy())
+            t0 = time.perf_counter()
+            tree = pyoracle.build(p)
+            build_s += time.perf_counter() - t0
+            self.built_points += p.shape[0]
+            self.trees.append({"node_aabbs": tree["node_aabbs"], "sorted_indices": tree["sorted_indices"]})
+            self.queries.append(np.ascontiguousarray(qs[b].numpy()))
+            if build_s > build_budget_s:
+                break
+        self.build_s = build_s
+        self.build_s_per_point = build_s / self.built_points
+        self._cursor = [0] * len(self.trees)
+        self.chunk = 2048
+
+    def step(self, budget_s: float) -> tuple[float, int]:
+        """Traverses fresh queries for about `budget_s` s; returns (seconds, queries)."""
+        done = 0
+        t0 = time.perf_counter()
+        while True:
+            for c, (tree, q) in enumerate(zip(self.trees, self.queries)):
+                s = self._cursor[c] % q.shape[0]
+                e = min(s + self.chunk, q.shape[0])
+                self._oracle.knn_reference(tree, q[s:e], self.w.k, threads=self.threads)
+                self._cursor[c] = e
+                done += e - s
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        return time.perf_counter() - t0, done
+
+    def estimate(self, seconds: float, queries: int) -> float:
+        build_parallel = min(self.threads, self.total_clouds)
+        est = (self.build_s_per_point * self.w.num_points / build_parallel
+               + seconds / queries * self.w.num_queries)
+        return self.w.num_queries / est
+
+    def describe(self, seconds: float, queries: int) -> str:
+        return (f"{len(self.trees)} of {self.total_clouds} clouds built in full ({self.built_points} points, "
+                f"{self.build_s:.2f} s on 1 thread), then {queries} of their queries traversed in {seconds:.2f} s on "
+                f"{self.threads} threads; extrapolated to the whole workload (build s/point x points / "
+                f"min(threads, clouds) + traversal s/query x queries); C restatement of the reference build + DFS "
+                f"traversal (oracle/tbvh_oracle.c)")
+
+
+def cpu_baseline(w, args, budget_s: float = 12.0) -> dict:
+    """`cpu_baseline` of the JSON line: the CPU port on a bounded sample (rank 0, one GPU)."""
+    sampler = CpuPortSample(w, build_budget_s=budget_s / 3)
+    seconds, queries = sampler.step(max(1.0, budget_s - sampler.build_s))
     return {
-        "value": m_total / est_s,
+        "value": sampler.estimate(seconds, queries),
         "unit": UNIT,
-        "cores": threads,
+        "cores": sampler.threads,
         "kind": "port",
-        "sample": (f"{clouds_used} of {len(sizes)} clouds built in full ({built_points} points), "
-                   f"{sampled_queries} queries traversed (first {per_cloud_q} per cloud); build time scaled by "
-                   f"points and query time by queries to the whole workload; C restatement of the reference "
-                   f"build + DFS traversal (oracle/tbvh_oracle.c), {threads} threads"),
-        "build_s_per_mpoints": build_per_point * 1e6,
-        "query_us_per_query": query_per_query * 1e6,
+        "extrapolated": True,
+        "sample": sampler.describe(seconds, queries),
+        "build_s_per_mpoints": sampler.build_s_per_point * 1e6,
+        "query_us_per_query": seconds / queries * 1e6,
     }
-
-
-def cpu_baseline(w, args) -> dict:
-    return cpu_port_throughput(w, args)
 
 
 def cpu_bruteforce_throughput(w, budget_s: float = 8.0, chunk_bytes: int = 1 << 28) -> dict:
@@ -677,7 +716,7 @@ def cpu_bruteforce_throughput(w, budget_s: float = 8.0, chunk_bytes: int = 1 << 
     prev = torch.get_num_threads()
     torch.set_num_threads(threads)
     try:
-        sizes, pts, qs = _cpu_sample(w, 0)
+        sizes, pts, qs = _cpu_sample(w)
         qcounts = ([int(q.shape[0]) for q in qs])
         est_s = 0.0
         sampled = 0
@@ -721,18 +760,26 @@ def cpu_bruteforce_throughput(w, budget_s: float = 8.0, chunk_bytes: int = 1 << 
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the CPU port of the reference algorithm (the reference's
+    k-NN path is CUDA-only), rank 0 only. Every step traverses a fresh bounded
+    query sample; the clouds are built once, before the first warm-up step."""
     if rank != 0:
         return None
     w = load_workload(args.workload, args)
-    vals = []
-    per_step_budget = max(2.0, 60.0 / max(1, args.steps + args.warmup))
-    cpu = None
+    t_build0 = time.perf_counter()
+    sampler = CpuPortSample(w)
+    build_wall = time.perf_counter() - t_build0
+    per_step_budget = max(0.5, 60.0 / max(1, args.steps + args.warmup))
+    vals, secs, counts = [], [], []
     for i in range(args.warmup + args.steps):
-        cpu = cpu_port_throughput(w, args, budget_s=per_step_budget)
+        seconds, queries = sampler.step(per_step_budget)
         if i >= args.warmup:
-            vals.append(cpu["value"])
+            vals.append(sampler.estimate(seconds, queries))
+            secs.append(seconds)
+            counts.append(queries)
     value = statistics.median(vals)
-    cpu["value"] = value
+    cpu = {"value": value, "unit": UNIT, "cores": sampler.threads, "kind": "port", "extrapolated": True,
+           "sample": sampler.describe(sum(secs), sum(counts))}
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -741,7 +788,11 @@ def run_reference(args, world, rank):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": w.num_queries / value * 1e3,
+        "ms_per_step": statistics.median(secs) * 1e3,
+        "extrapolated": True,
+        "queries_per_step": statistics.median(counts),
+        "measured_s": {"build_once": build_wall, "timed_steps": sum(secs)},
+        "estimated_ms_per_workload": w.num_queries / value * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -751,12 +802,18 @@ def run_reference(args, world, rank):
         "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("the reference's k-NN path is CUDA-only; this arm times the C restatement of its algorithm "
-                 "(oracle/) on the host cores"),
+                 "(oracle/) on the host cores. A step traverses a bounded sample of fresh queries "
+                 "(ms_per_step is that measured time); value extrapolates to the whole workload"),
     }
 
 
 def run_reference_cuda(args, world, rank, local):
-    """The reference's own CUDA path (baseline/_ref), timed exactly like the B200 arm's value."""
+    """The reference's own CUDA path (baseline/_ref), timed exactly like the B200 arm's value.
+
+    k = 32 (c4) is not offered by the reference's dispatch; there a step is the
+    reference's build and query sort plus its own traversal kernel instantiated
+    at K = 32 (oracle/ref_knn_harness.cu), labelled as such.
+    """
     ref_dir = ROOT / "baseline" / "_ref"
     if rank != 0:
         return None
@@ -768,37 +825,58 @@ def run_reference_cuda(args, world, rank, local):
     except Exception as exc:
         return {"impl": "reference_cuda", "unavailable": f"import failed: {exc}"}
     w = load_workload(args.workload, args)
-    if w.k not in ref.SUPPORTED_K:
-        return {"impl": "reference_cuda", "unavailable": f"k={w.k} not supported by the reference"}
     device = torch.device("cuda", local)
     points, queries = w.points.to(device), w.queries.to(device)
     offsets = w.batch_offsets.to(device) if w.batch_offsets is not None else None
     qoffsets = w.query_offsets.to(device) if w.query_offsets is not None else None
+    path = "reference public API: torchbvh.BVH(points).knn(queries, k)"
+    if w.k in ref.SUPPORTED_K:
+        def step():
+            bvh = ref.BVH(points, batch_offsets=offsets)
+            return bvh.knn(queries, w.k, query_offsets=qoffsets) if offsets is not None else bvh.knn(queries, w.k)
+    else:
+        if offsets is not None or points.dim() != 2:
+            return {"impl": "reference_cuda", "unavailable": f"k={w.k} not supported by the reference"}
+        from oracle import ref_harness
 
-    def step():
-        bvh = ref.BVH(points, batch_offsets=offsets)
-        return bvh.knn(queries, w.k, query_offsets=qoffsets) if offsets is not None else bvh.knn(queries, w.k)
+        harness = ref_harness.load()
+        path = (f"reference algorithm, K={w.k} instantiation (not a shipped reference path): reference "
+                f"build_bvh + morton_sort_queries_narrow + its traversal kernel template at K={w.k}")
 
+        def step():
+            h = ref.build_bvh(points)
+            order = ref._C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                                      h["scene_max"].unsqueeze(0))
+            return harness.knn_ordered_any_k(h["node_aabbs"].unsqueeze(0), h["sorted_indices"].unsqueeze(0),
+                                             queries.unsqueeze(0), order.contiguous(), int(h["num_leaves"]),
+                                             int(h["num_real_nodes"]), int(h["dim"]), w.k)
+
+    out = None
     for _ in range(args.warmup):
-        step()
+        out = step()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     torch.cuda.synchronize(device)
     ev = []
-    for _ in range(args.steps):
-        flush.zero_()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        step()
-        b.record(stream)
-        ev.append((a, b))
-    torch.cuda.synchronize(device)
+    sampler = ClockSampler(local)
+    with sampler:
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = step()
+            b.record(stream)
+            ev.append((a, b))
+        torch.cuda.synchronize(device)
+    del out
     total_ms = sum(a.elapsed_time(b) for a, b in ev)
     value = w.num_queries * args.steps / (total_ms / 1e3)
     return {"impl": "reference_cuda", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "config": workload_config(w, 1), "dtype": "f32",
+            "higher_is_better": True, "config": workload_config(w, 1), "dtype": "f32", "path": path,
+            "reference_version": getattr(ref, "__version__", None), "clocks": sampler.summary(),
+            "gpu": torch.cuda.get_device_name(device),
             "data": "synthetic (seeded CPU generator, torchbvh_b200.workloads)"}
 
 

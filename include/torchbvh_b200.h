@@ -102,8 +102,10 @@ int tbvh_sort_queries(int device, const float* queries, int64_t num_clouds, int6
  * Its scratch is a fixed array inside the library, held in the memory of
  * every GPU that loads the library until the process exits; one call sorts
  * at most 262,144 queries (larger calls return TBVH_ERR_BAD_ARG). The first
- * call on a device looks up that array's device address once, so make it
- * before any stream capture. Every call reuses the same array: the call
+ * call on a device looks up that array's device address once and keeps it for
+ * the life of the process, so make it before any stream capture; a device
+ * reset (cudaDeviceReset) is not supported afterwards. A negative `device`
+ * means the current device, as for tbvh_sort_queries. Every call reuses the same array: the call
  * clears what must start at zero, but calls that overlap on the GPU (other
  * streams, unordered host threads) race on it; keep them on one stream. */
 int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clouds, int64_t queries_per_cloud,

@@ -27,9 +27,15 @@ _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
 
 
+def reference_root() -> Path:
+    """The reference checkout: TORCHBVH_REFERENCE_ROOT, else a directory named
+    "reference" beside this repository (it need not exist)."""
+    return Path(os.environ.get("TORCHBVH_REFERENCE_ROOT", str(ORACLE_DIR.parent.parent / "reference")))
+
+
 def compile_libs(ref: bool = False) -> None:
     """Builds the oracle (and, when asked and the reference sources exist, the header shim)."""
-    targets = ["all"] + (["ref"] if ref else [])
+    targets = ["all"] + (["ref", f"REF_ROOT={reference_root()}"] if ref else [])
     subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), *targets], check=True)
 
 

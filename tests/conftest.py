@@ -26,21 +26,29 @@ def _gpu_explicitly_selected(config) -> bool:
     return "gpu" in expr and "notgpu" not in expr
 
 
+_NO_GPU_FAILS = False
+
+
 def pytest_collection_modifyitems(config, items):
+    global _NO_GPU_FAILS
     import torch
 
     if torch.cuda.is_available():
         return
     if _gpu_explicitly_selected(config):
-        fail = pytest.mark.xfail(reason="no CUDA device", run=False, strict=True)
-        for item in items:
-            if "gpu" in item.keywords:
-                item.add_marker(fail)
+        _NO_GPU_FAILS = True  # _gpu_required() fails every selected GPU test
         return
     skip = pytest.mark.skip(reason="needs a CUDA device")
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _gpu_required(request):
+    """With ``-m gpu`` and no CUDA device, every GPU test fails (never skips or xfails)."""
+    if _NO_GPU_FAILS and request.node.get_closest_marker("gpu") is not None:
+        pytest.fail("no CUDA device: a -m gpu run needs one")
 
 
 @pytest.fixture(scope="session")

@@ -119,3 +119,44 @@ def test_b200_knn_matches_reference_cuda(oracle, name):
         ok, msg = oracle.tie_equivalent(idx.cpu().numpy(), dist.cpu().numpy(), case["indices"], case["distances"])
         assert ok, msg
     assert torchbvh.device_status() == 0
+
+
+def _query_order_case(name: str) -> dict:
+    case = _case(name)
+    if "query_order" not in case:
+        pytest.skip("golden file predates the stored reference query permutation")
+    return case
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_query_order_vs_reference(oracle, name):
+    # The reference's own query permutation (_C.morton_sort_queries_narrow,
+    # torchbvh/csrc/morton_sort.cu:212-287) against the oracle's stable sort of
+    # Morton codes taken with the reference's scene bounds (same ulp caveat as
+    # the point order above).
+    case = _query_order_case(name)
+    q_all = case["queries"]
+    orders = case["query_order"]
+    lo_all, hi_all = case["scene_min"], case["scene_max"]
+    if q_all.ndim == 2:
+        q_all, orders, lo_all, hi_all = q_all[None], orders[None], lo_all[None], hi_all[None]
+    for q, order, lo, hi in zip(q_all, orders, lo_all, hi_all):
+        mine = oracle.stable_argsort(oracle.morton_codes(q, lo, hi))
+        mismatched = int(np.count_nonzero(mine != order))
+        assert mismatched <= max(4, q.shape[0] // 200), mismatched
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", CASES)
+def test_b200_query_order_matches_reference_cuda(name):
+    from torchbvh_b200._native import _C
+
+    case = _query_order_case(name)
+    q = torch.from_numpy(np.ascontiguousarray(case["queries"])).cuda()
+    lo = torch.from_numpy(case["scene_min"]).cuda()
+    hi = torch.from_numpy(case["scene_max"]).cuda()
+    if q.dim() == 2:
+        got = _C.morton_sort_queries_narrow(q[None], lo[None], hi[None])[0]
+    else:
+        got = _C.morton_sort_queries_narrow(q, lo, hi)
+    np.testing.assert_array_equal(got.cpu().numpy(), case["query_order"])

@@ -42,6 +42,13 @@ def _inputs():
     return big_p, big_q, bp, bq, rp, bo, rq, qo
 
 
+def _peer_query_sets(big_q):
+    """A different query set per reuse of the same PeerResults buffers, so stale or
+    racing rows from the previous call cannot pass as correct."""
+    g = torch.Generator().manual_seed(22)
+    return [big_q, big_q.flip(0).contiguous(), torch.rand(big_q.shape, generator=g)]
+
+
 def _worker(rank, world, port, outdir):
     import datetime
 
@@ -69,8 +76,8 @@ def _worker(rank, world, port, outdir):
         # Fused all-gather: each rank's traversal writes its rows into both
         # ranks' buffers over NVLink; the same buffers serve consecutive calls.
         peer = tdist.PeerResults(big_q.shape[0], 32, device=dev)
-        for rep, split in enumerate(("morton", "morton", "contiguous")):
-            i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, big_q.to(dev), 32,
+        for rep, (split, qset) in enumerate(zip(("morton", "morton", "contiguous"), _peer_query_sets(big_q))):
+            i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, qset.to(dev), 32,
                                                   num_points=big_p.shape[0], dim=3, device=dev, split=split,
                                                   out=peer)
             out[f"peer{rep}"] = (i.cpu().clone(), d.cpu().clone())
@@ -109,6 +116,7 @@ def test_sharded_knn_on_two_gpus_matches_one_gpu():
     dev = torch.device("cuda", 0)
     with torchbvh.BVH(big_p.to(dev)) as bvh:
         si, sd = bvh.knn(big_q.to(dev), 32)
+        peer_want = [tuple(t.cpu() for t in bvh.knn(qset.to(dev), 32)) for qset in _peer_query_sets(big_q)]
     with torchbvh.BVH(bp.to(dev)) as bvh:
         bi, bd = bvh.knn(bq.to(dev), 8)
     bot = torch.tensor(bo, device=dev)
@@ -123,7 +131,8 @@ def test_sharded_knn_on_two_gpus_matches_one_gpu():
         i, d, rows = got["single_none"]
         assert torch.equal(i, si.cpu()[rows]) and torch.equal(d, sd.cpu()[rows])
         for rep in range(3):
-            assert torch.equal(got[f"peer{rep}"][0], si.cpu()) and torch.equal(got[f"peer{rep}"][1], sd.cpu())
+            wi, wd = peer_want[rep]
+            assert torch.equal(got[f"peer{rep}"][0], wi) and torch.equal(got[f"peer{rep}"][1], wd)
         assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
         assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())
     shares = [torch.load(Path(outdir) / f"rank{r}.pt")["single_none"][2] for r in range(2)]

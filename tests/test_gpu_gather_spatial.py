@@ -115,3 +115,29 @@ def test_spatial_requires_an_order():
     with pytest.raises(RuntimeError, match="spatial"):
         _C.query_knn_batched_cached_bounds_spatial(bvh["node_aabbs"], bvh["sorted_indices"], points, None,
                                                     bvh["num_leaves"], bvh["num_real_nodes"], 3, 4)
+
+
+def test_spatial_rows_follow_the_reference_query_order(oracle):
+    """Spatial output (knn_query.cu:448-461): row p holds the result of the
+    reference's p-th query in its own Morton order (golden query_order)."""
+    from pathlib import Path
+
+    data = np.load(Path(__file__).resolve().parent / "golden" / "reference_cuda.npz")
+    if "rand_d3_n20000_k16/query_order" not in data.files:
+        pytest.skip("golden file predates the stored reference query permutation")
+    for name in ("rand_d3_n20000_k16", "rand_d2_n20000_k8", "gaussian_mixture_16384_k16"):
+        pts = torch.from_numpy(data[f"{name}/points"]).cuda()
+        q = torch.from_numpy(data[f"{name}/queries"]).cuda()
+        k = int(data[f"{name}/k"])
+        dim = pts.shape[1]
+        bvh = torchbvh.build_bvh(pts)
+        order = _C.morton_sort_queries_narrow(q[None], bvh["scene_min"][None], bvh["scene_max"][None]).contiguous()
+        s_idx, s_dist = _C.query_knn_batched_cached_bounds_spatial(
+            bvh["node_aabbs"][None], bvh["sorted_indices"][None], q[None], order, bvh["num_leaves"],
+            bvh["num_real_nodes"], dim, k)
+        ref_order = data[f"{name}/query_order"]
+        want_idx = data[f"{name}/indices"][ref_order]
+        want_dist = data[f"{name}/distances"][ref_order]
+        ok, msg = oracle.tie_equivalent(s_idx[0].cpu().numpy(), s_dist[0].cpu().numpy(), want_idx, want_dist)
+        assert ok, f"{name}: {msg}"
+    assert torchbvh.device_status() == 0

@@ -58,6 +58,30 @@ def test_share_in_given_order_matches_too():
         _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 4096, queries, share, 16,
                                 [di.data_ptr()], [dd.data_ptr()])
     assert torch.equal(di, ref_idx) and torch.equal(dd, ref_dist)
+    assert torchbvh.device_status() == 0
+
+
+def test_share_with_an_out_of_range_index_sets_the_status_bit():
+    """A share entry outside [0, num_queries) is clamped to query 0 (so every read and
+    write stays in bounds) and raises TBVH_DEVICE_BAD_INDEX; the valid rows are exact."""
+    points = _cloud(9, (4096, 3))
+    queries = _cloud(10, (1500, 3))
+    assert torchbvh.device_status() == 0
+    with torchbvh.BVH(points) as bvh:
+        h = bvh._handle
+        ref_idx, ref_dist = bvh.knn(queries, 8)
+        di = torch.full((1500, 8), -7, dtype=torch.int64, device="cuda")
+        dd = torch.full((1500, 8), -7.0, device="cuda")
+        share = torch.tensor([5, 1500, 7, -3], dtype=torch.int64, device="cuda")
+        _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 4096, queries, share, 8,
+                                [di.data_ptr()], [dd.data_ptr()])
+        torch.cuda.synchronize()
+    assert torchbvh.device_status() == _native.TBVH_DEVICE_BAD_INDEX
+    for row in (0, 5, 7):
+        assert torch.equal(di[row], ref_idx[row]) and torch.equal(dd[row], ref_dist[row])
+    untouched = torch.ones(1500, dtype=torch.bool, device="cuda")
+    untouched[[0, 5, 7]] = False
+    assert bool((di[untouched] == -7).all()) and bool((dd[untouched] == -7.0).all())
 
 
 def test_peer_buffer_round_trip_on_one_device():

@@ -7,7 +7,9 @@ memory at start-up). Its scratch is a fixed array inside the library, shared
 by every call, so the test makes two calls in a row with different inputs:
 each must equal the workspace version's output exactly (integer
 permutation), which also shows nothing left over from the first call leaks
-into the second. Collected last so a first-failure stop has run the rest.
+into the second. A second test checks consecutive calls against the
+reference's own query permutation stored in the golden vectors. Collected
+last so a first-failure stop has run the rest.
 """
 
 from __future__ import annotations
@@ -103,3 +105,32 @@ def test_noalloc_sort_rejects_more_than_its_capacity():
                                        torch.cuda.current_stream().cuda_stream)
     assert rc == _native.TBVH_ERR_BAD_ARG
     assert b"static scratch capacity" in lib.tbvh_last_error()
+
+
+def test_noalloc_sort_matches_reference_permutation():
+    """Two calls in a row on golden cases: each output must equal the reference's own
+    query permutation (its morton_sort_queries_narrow, stored by the golden generator)."""
+    from pathlib import Path
+
+    golden = Path(__file__).resolve().parent / "golden" / "reference_cuda.npz"
+    data = np.load(golden)
+    if "c1/query_order" not in data.files:
+        pytest.skip("golden file predates the stored reference query permutation")
+    lib = _lib()
+    for name in ("c1", "rand_d2_n20000_k8", "batched_3x3000_k8", "rand_d3_n20000_k16"):
+        if name == "c1":
+            from torchbvh_b200 import workloads
+
+            q = workloads.c1_single_uniform().queries.numpy()
+        else:
+            q = data[f"{name}/queries"]
+        want = data[f"{name}/query_order"]
+        qt = torch.from_numpy(np.ascontiguousarray(q)).cuda()
+        lo = torch.from_numpy(np.ascontiguousarray(data[f"{name}/scene_min"])).cuda().reshape(-1, q.shape[-1])
+        hi = torch.from_numpy(np.ascontiguousarray(data[f"{name}/scene_max"])).cuda().reshape(-1, q.shape[-1])
+        clouds = lo.shape[0]
+        per_cloud = q.shape[-2]
+        got = _noalloc_sort(lib, qt, clouds, per_cloud, None, clouds * per_cloud, q.shape[-1], lo, hi)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got.cpu().numpy().reshape(want.shape), want)
+    assert _native.device_status() == 0

@@ -35,6 +35,12 @@ TBVH_ERR_UNSUPPORTED_K = 2
 TBVH_ERR_CUDA = 3
 TBVH_ERR_WORKSPACE = 4
 
+# Device status bits (tbvh_device_status).
+TBVH_DEVICE_LOOKBACK_TIMEOUT = 1
+TBVH_DEVICE_STACK_OVERFLOW = 2
+TBVH_DEVICE_TREE_COUNTER = 4
+TBVH_DEVICE_BAD_INDEX = 8
+
 _lib = None
 _lib_lock = threading.Lock()
 

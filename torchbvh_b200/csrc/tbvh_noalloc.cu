@@ -14,7 +14,9 @@
 //
 // One-time set-up per device: the first call on a device (with that device
 // current) resolves the array's device address with cudaGetSymbolAddress and
-// caches it. Make that first call before any stream capture.
+// caches it for the life of the process. Make that first call before any
+// stream capture. A device reset (cudaDeviceReset) invalidates the cached
+// address and is not supported while this library is loaded.
 //
 // All calls share the one array and it keeps whatever the last call left in
 // it. The launch sequence clears what must start at zero (digit histograms,
@@ -97,7 +99,13 @@ int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clou
     return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: ragged queries need device offsets", op);
   if (queries_per_cloud > 0 && queries_per_cloud * num_clouds != total_queries)
     return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: queries_per_cloud * num_clouds != total_queries", op);
-  if (device < 0 || device >= kMaxDevices) return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: bad device ordinal", op);
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (device < 0) {  // as in tbvh_sort_queries: a negative ordinal means the current device
+    if (e != cudaSuccess) return noalloc_fail(TBVH_ERR_CUDA, "%s: cudaGetDevice: %s", op, cudaGetErrorString(e));
+    device = cur;
+  }
+  if (device >= kMaxDevices) return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: bad device ordinal", op);
   if (total_queries == 0) return TBVH_OK;
   if (!queries || !scene_min || !scene_max || !order_out)
     return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: NULL input/output pointer", op);
@@ -105,8 +113,6 @@ int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clou
   if (tbvh::sort_scratch_bytes(plan) > kNoAllocScratchBytes)
     return noalloc_fail(TBVH_ERR_BAD_ARG, "%s: scratch plan exceeds the static array", op);
 
-  int cur = -1;
-  cudaError_t e = cudaGetDevice(&cur);
   if (e != cudaSuccess || cur != device) {
     e = cudaSetDevice(device);
     if (e != cudaSuccess) return noalloc_fail(TBVH_ERR_CUDA, "%s: cudaSetDevice: %s", op, cudaGetErrorString(e));

@@ -103,9 +103,12 @@ class PeerResults:
     result row of its share into all ranks' buffers (NVLink stores) as the rows
     are produced, instead of an NCCL all-gather after the traversal.
     ``indices`` / ``distances`` are this rank's (M, k) buffers; a call
-    overwrites them, so read (or copy) the results before the next call with
-    the same object. Create once, reuse across calls, ``close()`` on every
-    rank together (a collective).
+    overwrites them. Each call begins with a collective on every rank's current
+    stream before any rank writes, so reads of the previous results enqueued on
+    the current stream (or finished on the host) are safe on every rank; reads
+    on other streams must be ordered before the next call by the caller.
+    Create once, reuse across calls, ``close()`` on every rank together (a
+    collective).
     """
 
     def __init__(self, num_queries: int, k: int, *, group=None, device: torch.device | None = None):
@@ -180,6 +183,10 @@ def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, q0: int
             share = order[q0:q1]
         else:
             share = torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
+        # No rank may store into a peer's buffers while that peer still reads the
+        # previous call's rows: a collective on every rank's current stream, after
+        # its earlier reads and before any traversal, orders them.
+        out.delivered()
         query_knn_share(h["node_aabbs"], h["sorted_indices"], points.shape[0], queries, share, k,
                         out.dest_indices, out.dest_distances)
     out.delivered()
