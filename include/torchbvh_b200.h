@@ -80,6 +80,14 @@ int tbvh_build(int device, const float* points, int64_t num_clouds, int64_t poin
                int traversal_arrays_per_cloud,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Traversal arrays of one cloud of num_points points: left_child_mem,
+ * right_child_mem, mem_to_leaf int32 [tbvh_real_node_count(num_points)], the
+ * values build_traversal_arrays_kernel writes (torchbvh/csrc/bvh_build.cu:
+ * 361-398). They depend on num_points only, so a caller may pass NULL for
+ * them to tbvh_build and compute them here when they are first read. */
+int tbvh_traversal_arrays(int device, int64_t num_points, int32_t* left_child_mem, int32_t* right_child_mem,
+                          int32_t* mem_to_leaf, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Morton permutation of query points. Replaces morton_sort_queries_narrow_cuda
  * (torchbvh/csrc/morton_sort.cu:264-287, bound as morton_sort_queries_narrow in

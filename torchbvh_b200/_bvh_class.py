@@ -1,12 +1,19 @@
-"""``BVH`` class (torchbvh/_bvh_class.py:14-105), k-NN surface only."""
+"""``BVH``: the object-style entry point (torchbvh/_bvh_class.py:14-105, k-NN part).
+
+``BVH(points[, batch_offsets=...])`` builds at construction through
+``build_bvh`` (same dispatch: (N, D) single, (B, N, D) batched, packed
+(total_N, D) with offsets ragged), ``.knn(...)`` forwards to ``query_knn``,
+and the object owns its handle: ``destroy()`` / ``with`` release it. The
+handle's fields stay private (the class is not a mapping).
+"""
 
 from __future__ import annotations
 
 import torch
 
-from ._handles import BVHHandle, BatchedBVHHandle, RaggedBVHHandle, destroy_bvh
-from ._query import _build_bvh_batched, _build_bvh_ragged, _build_bvh_single, query_knn
-from ._validation import _as_contiguous, _as_contiguous_int64
+from ._handles import destroy_bvh
+from ._query import build_bvh, query_knn
+from ._validation import _reject_unless
 
 
 class BVH:
@@ -18,52 +25,30 @@ class BVH:
       -> ragged packed BVH
 
     Owns handle lifetime. Supports the context-manager protocol.
-    Does not expose internal handle fields.
     """
 
     def __init__(self, points: torch.Tensor, *, batch_offsets: torch.Tensor | None = None) -> None:
+        # The class reports shape problems under its own name before building.
         if batch_offsets is not None:
-            if points.dim() != 2:
-                raise ValueError("BVH: ragged mode requires 2-D points (total_N, D)")
-            points = _as_contiguous(points)
-            batch_offsets = _as_contiguous_int64(batch_offsets)
-            self._handle: BVHHandle | BatchedBVHHandle | RaggedBVHHandle = _build_bvh_ragged(points, batch_offsets)
-        elif points.dim() == 3:
-            points = _as_contiguous(points)
-            self._handle = _build_bvh_batched(points)
-        elif points.dim() == 2:
-            points = _as_contiguous(points)
-            self._handle = _build_bvh_single(points)
+            _reject_unless(points.dim() == 2, "BVH: ragged mode requires 2-D points (total_N, D)")
         else:
-            raise ValueError("BVH: points must have shape (N, D) or (B, N, D)")
+            _reject_unless(points.dim() in (2, 3), "BVH: points must have shape (N, D) or (B, N, D)")
+        self._handle = build_bvh(points, batch_offsets=batch_offsets)
         self._points = points
 
     @property
     def destroyed(self) -> bool:
         return self._handle.destroyed
 
-    def knn(
-        self,
-        query_points: torch.Tensor,
-        k: int,
-        *,
-        query_offsets: torch.Tensor | None = None,
-        source_points: torch.Tensor | None = None,
-        sort_queries: bool = True,
-    ):
-        """Query k nearest neighbors.
+    def knn(self, query_points: torch.Tensor, k: int, *, query_offsets: torch.Tensor | None = None,
+            source_points: torch.Tensor | None = None, sort_queries: bool = True):
+        """Query k nearest neighbors (see ``query_knn``).
 
         For ragged BVHs ``query_offsets`` is required. For single/batched BVHs
         ``sort_queries`` controls Morton-sorted traversal (default True).
         """
-        return query_knn(
-            self._handle,
-            query_points,
-            k,
-            query_offsets=query_offsets,
-            source_points=source_points,
-            sort_queries=sort_queries,
-        )
+        return query_knn(self._handle, query_points, k, query_offsets=query_offsets, source_points=source_points,
+                         sort_queries=sort_queries)
 
     def destroy(self) -> None:
         destroy_bvh(self._handle)
@@ -71,5 +56,5 @@ class BVH:
     def __enter__(self) -> "BVH":
         return self
 
-    def __exit__(self, *args) -> None:
+    def __exit__(self, *exc) -> None:
         self.destroy()

@@ -1,14 +1,18 @@
-"""Python-owned BVH handles.
+"""BVH handles: the Python objects ``build_bvh`` returns.
 
-Same contract as torchbvh/_handles.py:7-120: Mapping access to the tensor
-payload, a ``destroyed`` flag, idempotent ``destroy()``, ``RuntimeError`` on
-use after destroy, cascade destroy for ragged handles, ``TypeError`` for
-foreign objects.
+Contract kept from torchbvh (torchbvh/_handles.py:7-120): a handle is a
+read-only ``Mapping`` over its payload, ``destroyed`` tells whether it was
+released, ``destroy()`` is idempotent and drops the tensor references, any
+later access raises ``RuntimeError`` with the handle kind's message, a ragged
+handle destroys its per-sample handles with it, and helpers reject foreign
+objects with ``TypeError``.
 
-Ragged handles additionally keep the packed device payload of one on-device
-build (``_packed``); their per-sample ``BVHHandle`` views are materialised
-lazily so that building 64 clouds does not cost 64 Python dictionaries of
-tensor views unless a caller asks for them.
+Design here: a payload field may be *deferred* — stored as a ``_Deferred``
+thunk and computed on first read, then kept. Builds use that for the
+traversal arrays (``left_child_mem`` / ``right_child_mem`` / ``mem_to_leaf``,
+which depend only on the point count and which the k-NN path never reads) and
+ragged builds for their per-sample handles, which are views into one packed
+payload materialised only when a caller asks for them.
 """
 
 from __future__ import annotations
@@ -19,122 +23,140 @@ from contextlib import contextmanager
 import torch
 
 
-class _MappingBVHHandle(Mapping):
-    """Shared mapping/liveness behaviour for Python-owned BVH handles."""
+class _Deferred:
+    """A payload field computed on first read."""
 
-    _destroyed_message = "BVH handle has been destroyed"
+    __slots__ = ("make",)
 
-    def __init__(self, data: Mapping, *, marker: str | None = None):
-        self._data = dict(data)
-        if marker is not None:
-            self._data[marker] = True
-        self._destroyed = False
+    def __init__(self, make: Callable[[], object]):
+        self.make = make
+
+
+class _Handle(Mapping):
+    kind_message = "BVH handle has been destroyed"
+    marker: str | None = None
+
+    def __init__(self, fields: Mapping):
+        self._fields = dict(fields)
+        if self.marker is not None:
+            self._fields[self.marker] = True
+        self._alive = True
 
     @property
     def destroyed(self) -> bool:
-        return self._destroyed
+        return not self._alive
 
     def destroy(self) -> None:
-        self._destroyed = True
-        self._data.clear()
+        self._alive = False
+        self._fields = {}
+
+    def _live_fields(self) -> dict:
+        if not self._alive:
+            raise RuntimeError(self.kind_message)
+        return self._fields
 
     def _require_live(self) -> dict:
-        if self._destroyed:
-            raise RuntimeError(self._destroyed_message)
-        return self._data
+        """The raw payload (deferred fields not computed): what the query paths read."""
+        return self._live_fields()
 
     def __getitem__(self, key):
-        return self._require_live()[key]
+        fields = self._live_fields()
+        value = fields[key]
+        if isinstance(value, _Deferred):
+            value = fields[key] = value.make()
+        return value
 
     def __iter__(self) -> Iterator:
-        return iter(self._require_live())
+        return iter(list(self._live_fields()))
 
     def __len__(self) -> int:
-        return len(self._require_live())
+        return len(self._live_fields())
 
 
-class BVHHandle(_MappingBVHHandle):
-    """Lifecycle wrapper around one cloud's BVH payload."""
+class BVHHandle(_Handle):
+    """One cloud's BVH payload."""
 
 
 class _LazyBVHHandle(BVHHandle):
-    """Per-sample handle of a ragged build whose payload is built on first use."""
+    """A per-sample handle of a ragged build: its whole payload comes from
+    `factory` on first access."""
 
     def __init__(self, factory: Callable[[], Mapping]):
         super().__init__({})
         self._factory: Callable[[], Mapping] | None = factory
 
-    def _require_live(self) -> dict:
-        data = super()._require_live()
+    def _live_fields(self) -> dict:
+        fields = super()._live_fields()
         if self._factory is not None:
-            data.update(self._factory())
+            fields.update(self._factory())
             self._factory = None
-        return data
+        return fields
 
     def destroy(self) -> None:
         self._factory = None
         super().destroy()
 
 
-class BatchedBVHHandle(_MappingBVHHandle):
-    """Lifecycle wrapper around a fixed-size batched BVH payload."""
+class BatchedBVHHandle(_Handle):
+    """Fixed-size batch of BVHs (leading batch dimension on every tensor field)."""
 
-    _destroyed_message = "Batched BVH handle has been destroyed"
-
-    def __init__(self, data: Mapping):
-        super().__init__(data, marker="_batched")
+    kind_message = "Batched BVH handle has been destroyed"
+    marker = "_batched"
 
 
-class RaggedBVHHandle(_MappingBVHHandle):
-    """Lifecycle wrapper around packed ragged metadata, payload and sample handles."""
+class RaggedBVHHandle(_Handle):
+    """Ragged batch: metadata fields, per-sample handles (``_handles``) and the
+    packed payload of the one native build behind them."""
 
-    _destroyed_message = "Ragged BVH handle has been destroyed"
+    kind_message = "Ragged BVH handle has been destroyed"
+    marker = "_ragged"
 
-    def __init__(self, data: Mapping, handles: list[BVHHandle], packed: Mapping | None = None):
-        super().__init__(data, marker="_ragged")
+    def __init__(self, fields: Mapping, handles: list[BVHHandle], packed: Mapping | None = None):
+        super().__init__(fields)
         self._handles = list(handles)
-        self._packed = dict(packed) if packed is not None else {}
+        self._packed = dict(packed or {})
 
     def destroy(self) -> None:
-        if not self._destroyed:
-            for handle in self._handles:
-                handle.destroy()
-        self._destroyed = True
-        self._handles.clear()
-        self._packed.clear()
-        self._data.clear()
+        if self._alive:
+            for inner in self._handles:
+                inner.destroy()
+        self._handles = []
+        self._packed = {}
+        super().destroy()
 
     def _require_handles(self) -> list[BVHHandle]:
-        self._require_live()
+        self._live_fields()
         return self._handles
 
     def _require_packed(self) -> dict:
-        self._require_live()
+        self._live_fields()
         return self._packed
 
 
-def _bvh_data(bvh, prefix: str = "query_knn") -> Mapping:
-    if isinstance(bvh, (BatchedBVHHandle, RaggedBVHHandle)):
-        raise TypeError(f"{prefix}: bvh must be a BVHHandle returned by build_bvh")
-    if isinstance(bvh, BVHHandle):
+def _payload_of(bvh, expected: type, prefix: str, what: str) -> Mapping:
+    """Live payload of `bvh` if it is a handle of the expected kind (the three
+    kinds are unrelated classes, so a batched or ragged handle never passes
+    for a single one)."""
+    if isinstance(bvh, expected):
         return bvh._require_live()
-    raise TypeError(f"{prefix}: bvh must be a BVHHandle returned by build_bvh")
+    raise TypeError(f"{prefix}: bvh must be a {what} returned by build_bvh")
+
+
+def _bvh_data(bvh, prefix: str = "query_knn") -> Mapping:
+    return _payload_of(bvh, BVHHandle, prefix, "BVHHandle")
 
 
 def _batched_bvh_data(bvh, prefix: str = "query_knn") -> Mapping:
-    if isinstance(bvh, BatchedBVHHandle):
-        return bvh._require_live()
-    raise TypeError(f"{prefix}: bvh must be a BatchedBVHHandle returned by build_bvh")
+    return _payload_of(bvh, BatchedBVHHandle, prefix, "BatchedBVHHandle")
 
 
 def _ragged_bvh_data(bvh, prefix: str = "query_knn") -> tuple[Mapping, dict]:
-    if isinstance(bvh, RaggedBVHHandle):
-        return bvh._require_live(), bvh._require_packed()
-    raise TypeError(f"{prefix}: bvh must be a RaggedBVHHandle returned by build_bvh")
+    return _payload_of(bvh, RaggedBVHHandle, prefix, "RaggedBVHHandle"), bvh._require_packed()
 
 
 @contextmanager
 def _temporary_bvh(build_fn, points: torch.Tensor):
+    """A handle from `build_fn(points)` that is destroyed when the block exits."""
     handle = build_fn(points)
     try:
         yield handle
@@ -144,7 +166,6 @@ def _temporary_bvh(build_fn, points: torch.Tensor):
 
 def destroy_bvh(bvh: BVHHandle | BatchedBVHHandle | RaggedBVHHandle) -> None:
     """Destroy a Python BVH handle and release its tensor references."""
-    if isinstance(bvh, (RaggedBVHHandle, BatchedBVHHandle, BVHHandle)):
-        bvh.destroy()
-        return
-    raise TypeError("destroy_bvh: bvh must be a handle returned by build_bvh")
+    if not isinstance(bvh, _Handle):
+        raise TypeError("destroy_bvh: bvh must be a handle returned by build_bvh")
+    bvh.destroy()

@@ -59,6 +59,7 @@ _SIGNATURES = {
         _i32,
         [_i32, _ptr, _i64, _i64, _ptr, _ptr, _i32, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i32, _ptr, _size, _ptr],
     ),
+    "tbvh_traversal_arrays": (_i32, [_i32, _i64, _ptr, _ptr, _ptr, _ptr]),
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),
@@ -144,6 +145,37 @@ def _tree_scalars(n: int) -> dict:
     }
 
 
+def traversal_arrays(num_points: int, device: torch.device) -> dict:
+    """left_child_mem / right_child_mem / mem_to_leaf int32 of one cloud of
+    `num_points` points (bvh_build.cu:361-398 values), computed on `device`."""
+    lib = load_library()
+    rows = real_node_count(num_points)
+    out = {key: torch.empty((rows,), dtype=torch.int32, device=device)
+           for key in ("left_child_mem", "right_child_mem", "mem_to_leaf")}
+    _check(lib.tbvh_traversal_arrays(device.index, int(num_points), out["left_child_mem"].data_ptr(),
+                                     out["right_child_mem"].data_ptr(), out["mem_to_leaf"].data_ptr(),
+                                     _stream(device)))
+    return out
+
+
+def deferred_traversal_arrays(num_points: int, device: torch.device) -> dict:
+    """The three traversal-array payload fields as deferred entries: the k-NN
+    path never reads them and they depend only on the point count, so they are
+    computed (once, together) when a caller first reads one of them."""
+    from ._handles import _Deferred
+
+    made: dict = {}
+
+    def field(key):
+        def make():
+            if not made:
+                made.update(traversal_arrays(num_points, device))
+            return made[key]
+        return _Deferred(make)
+
+    return {key: field(key) for key in ("left_child_mem", "right_child_mem", "mem_to_leaf")}
+
+
 def device_status(device: int | torch.device | None = None, clear: bool = True) -> int:
     """Error bits raised by bounded device waits (0 when healthy). Synchronises."""
     lib = load_library()
@@ -177,15 +209,12 @@ def build_bvh_batched_cooperative(points: torch.Tensor) -> dict:
     sorted_indices = torch.empty((batch, n), dtype=torch.int64, device=device)
     scene_min = torch.empty((batch, dim), dtype=torch.float32, device=device)
     scene_max = torch.empty((batch, dim), dtype=torch.float32, device=device)
-    left = torch.empty((nr,), dtype=torch.int32, device=device)
-    right = torch.empty((nr,), dtype=torch.int32, device=device)
-    m2l = torch.empty((nr,), dtype=torch.int32, device=device)
     ws_bytes = lib.tbvh_build_workspace_size(batch, n, None, dim)
     ws = _workspace(ws_bytes, device)
     _check(lib.tbvh_build(
         device.index, points.data_ptr(), batch, n, None, None, dim,
         node_aabbs.data_ptr(), sorted_indices.data_ptr(), scene_min.data_ptr(), scene_max.data_ptr(),
-        left.data_ptr(), right.data_ptr(), m2l.data_ptr(), 0,
+        None, None, None, 0,
         ws.data_ptr(), ws.numel(), _stream(device),
     ))
     out = {
@@ -195,9 +224,8 @@ def build_bvh_batched_cooperative(points: torch.Tensor) -> dict:
         "scene_max": scene_max,
         "batch_size": batch,
         "dim": dim,
-        "left_child_mem": left,
-        "right_child_mem": right,
-        "mem_to_leaf": m2l,
+        # One shared set for every cloud of the batch (they have the same size).
+        **deferred_traversal_arrays(n, device),
     }
     out.update(_tree_scalars(n))
     return out
@@ -225,16 +253,13 @@ def build_bvh_ragged(points: torch.Tensor, batch_offsets: torch.Tensor, offsets:
     sorted_indices = torch.empty((offsets[-1],), dtype=torch.int64, device=device)
     scene_min = torch.empty((clouds, dim), dtype=torch.float32, device=device)
     scene_max = torch.empty((clouds, dim), dtype=torch.float32, device=device)
-    left = torch.empty((row_offsets[-1],), dtype=torch.int32, device=device)
-    right = torch.empty((row_offsets[-1],), dtype=torch.int32, device=device)
-    m2l = torch.empty((row_offsets[-1],), dtype=torch.int32, device=device)
     host_offsets = (ctypes.c_int64 * len(offsets))(*offsets)
     ws_bytes = lib.tbvh_build_workspace_size(clouds, 0, ctypes.cast(host_offsets, _ptr), dim)
     ws = _workspace(ws_bytes, device)
     _check(lib.tbvh_build(
         device.index, points.data_ptr(), clouds, 0, batch_offsets.data_ptr(), ctypes.cast(host_offsets, _ptr), dim,
         node_aabbs.data_ptr(), sorted_indices.data_ptr(), scene_min.data_ptr(), scene_max.data_ptr(),
-        left.data_ptr(), right.data_ptr(), m2l.data_ptr(), 1,
+        None, None, None, 1,
         ws.data_ptr(), ws.numel(), _stream(device),
     ))
     return {
@@ -242,9 +267,6 @@ def build_bvh_ragged(points: torch.Tensor, batch_offsets: torch.Tensor, offsets:
         "sorted_indices": sorted_indices,
         "scene_min": scene_min,
         "scene_max": scene_max,
-        "left_child_mem": left,
-        "right_child_mem": right,
-        "mem_to_leaf": m2l,
         "row_offsets": row_offsets,
         "point_offsets": list(offsets),
         "point_offsets_device": batch_offsets,
@@ -525,4 +547,6 @@ _C = types.SimpleNamespace(
     build_bvh_ragged=build_bvh_ragged,
     morton_sort_queries_ragged=morton_sort_queries_ragged,
     query_knn_ragged=query_knn_ragged,
+    tree_scalars=_tree_scalars,
+    deferred_traversal_arrays=deferred_traversal_arrays,
 )

@@ -1,12 +1,19 @@
-"""Build and query orchestration (torchbvh/_query.py:29-405, same contracts).
+"""Build and query orchestration behind ``build_bvh`` / ``query_knn`` / ``BVH``.
 
-Single and fixed-size batched calls go through the reference-named ``_C``
-functions exactly like the reference (single = batched with B = 1, then the
-batch dimension is squeezed). Ragged calls differ in mechanism only: the
-reference loops over samples in Python (one build and one query per sample,
-then ``torch.cat``); here every sample is built and queried in one native
-launch sequence over the packed tensors. Public results, shapes, local
-indices and error messages are unchanged.
+Contract kept from torchbvh (torchbvh/_query.py:29-405): the same dispatch on
+input shape and handle kind, the same payload fields, result shapes, local
+indices, exception types and messages, and the same reference-named ``_C``
+functions on the single and fixed-size batched paths.
+
+Organisation here: every call resolves to one of three cloud layouts —
+``single`` (one (N, D) cloud), ``batched`` (B clouds of N points) or
+``ragged`` (packed clouds with offsets). A layout is a row of rule tables
+(which argument shapes it accepts and what it says when they are wrong) plus
+one native path. Single clouds run the batched native path with B = 1.
+Ragged input is one packed native build and one packed query over all clouds
+(the reference builds and queries each sample in a Python loop and
+concatenates); per-sample handles are views into the packed payload, made on
+first access.
 """
 
 from __future__ import annotations
@@ -29,6 +36,7 @@ from ._native import _C
 from ._validation import (
     _as_contiguous,
     _as_contiguous_int64,
+    _reject_unless,
     _validate_cuda_float32,
     _validate_offsets,
     _validate_ragged_points,
@@ -36,65 +44,126 @@ from ._validation import (
 )
 
 _INT32_MAX = 2**31 - 1
+_SINGLE, _BATCHED, _RAGGED = "single", "batched", "ragged"
 
 
 def _validate_narrow_build_extent(prefix: str, points: torch.Tensor) -> None:
-    # Indices and sort values are 32-bit inside the native path (as in the reference).
-    total = int(points.size(0)) if points.dim() == 2 else int(points.size(0)) * int(points.size(1))
-    if total > _INT32_MAX:
-        raise ValueError(f"{prefix}: total point count must fit in signed int32")
+    # Point indices and sort values are 32-bit inside the native path.
+    total = points.numel() // max(int(points.size(-1)), 1)
+    _reject_unless(total <= _INT32_MAX, f"{prefix}: total point count must fit in signed int32")
+
+
+# ---------------------------------------------------------------------------
+# Rule tables. Each entry is (holds(tensor, payload), message); they run in order.
+# ---------------------------------------------------------------------------
+
+_BUILD_RULES = {
+    _SINGLE: (
+        (lambda p: p.dim() == 2, "build_bvh: points must have shape (N, D)"),
+        (lambda p: p.size(1) in SUPPORTED_DIMS, "build_bvh: D must be 2 or 3"),
+    ),
+    _BATCHED: (
+        (lambda p: p.dim() == 3, "build_bvh: batched points must have shape (B, N, D)"),
+        (lambda p: p.size(2) in SUPPORTED_DIMS, "build_bvh: D must be 2 or 3"),
+    ),
+}
+
+_QUERY_SHAPE_RULES = {
+    _SINGLE: (
+        (lambda q, d: q.dim() == 2, "query_knn: query_points must have shape (M, D)"),
+        (lambda q, d: q.size(1) == d["dim"], "query_knn: query_points second dimension must match BVH dim"),
+    ),
+    _BATCHED: (
+        (lambda q, d: q.dim() == 3, "query_knn: batched query_points must have shape (B, M, D)"),
+        (lambda q, d: q.size(0) == d["batch_size"], "query_knn: query_points batch size must match BVH batch_size"),
+        (lambda q, d: q.size(2) == d["dim"], "query_knn: query_points last dimension must match BVH dim"),
+    ),
+    _RAGGED: (
+        (lambda q, d: q.dim() == 2, "query_knn: ragged query_points must have shape (total_M, D)"),
+        (lambda q, d: q.size(1) == d["dim"], "query_knn: query_points second dimension must match BVH dim"),
+    ),
+}
+
+# Source-point rules take the payload's size facts: (num_leaves or total_N, batch_size, dim).
+_SOURCE_SHAPE_RULES = {
+    _SINGLE: (
+        (lambda s, n, b, d: s.dim() == 2, "source_points must have shape (N, D)"),
+        (lambda s, n, b, d: s.size(0) == n, "source_points first dimension must match BVH num_leaves"),
+        (lambda s, n, b, d: s.size(1) == d, "source_points second dimension must match BVH dim"),
+    ),
+    _BATCHED: (
+        (lambda s, n, b, d: s.dim() == 3, "source_points must have shape (B, N, D)"),
+        (lambda s, n, b, d: s.size(0) == b, "source_points batch size must match BVH batch_size"),
+        (lambda s, n, b, d: s.size(1) == n, "source_points second dimension must match BVH num_leaves"),
+        (lambda s, n, b, d: s.size(2) == d, "source_points last dimension must match BVH dim"),
+    ),
+    _RAGGED: (
+        (lambda s, n, b, d: s.dim() == 2, "ragged source_points must have shape (total_N, D)"),
+        (lambda s, n, b, d: s.size(0) == n, "source_points first dimension must match BVH total_N"),
+        (lambda s, n, b, d: s.size(1) == d, "source_points second dimension must match BVH dim"),
+    ),
+}
+
+
+def _check_source_points(layout: str, prefix: str, source: torch.Tensor, rows: int, batch: int | None, dim: int,
+                         device: torch.device) -> torch.Tensor:
+    for holds, text in _SOURCE_SHAPE_RULES[layout]:
+        _reject_unless(holds(source, rows, batch, dim), f"{prefix}: {text}")
+    _validate_cuda_float32(prefix, source, "source_points")
+    _reject_unless(source.device == device, f"{prefix}: source_points must be on the same device as the BVH")
+    return _as_contiguous(source)
+
+
+def _validate_single_source_points(prefix: str, data: Mapping, source_points: torch.Tensor) -> None:
+    _check_source_points(_SINGLE, prefix, source_points, data["num_leaves"], None, data["dim"],
+                         data["sorted_indices"].device)
+
+
+def _validate_batched_source_points(prefix: str, data: Mapping, source_points: torch.Tensor) -> None:
+    _check_source_points(_BATCHED, prefix, source_points, data["num_leaves"], data["batch_size"], data["dim"],
+                         data["sorted_indices"].device)
 
 
 # ---------------------------------------------------------------------------
 # Builders
 # ---------------------------------------------------------------------------
 
-def _build_bvh_single(points: torch.Tensor) -> BVHHandle:
-    if points.dim() != 2:
-        raise ValueError("build_bvh: points must have shape (N, D)")
-    if points.size(1) not in SUPPORTED_DIMS:
-        raise ValueError("build_bvh: D must be 2 or 3")
+def _checked_build_points(layout: str, points: torch.Tensor) -> torch.Tensor:
+    for holds, text in _BUILD_RULES[layout]:
+        _reject_unless(holds(points), text)
     _validate_cuda_float32("build_bvh", points, "points")
     points = _as_contiguous(points)
     _validate_narrow_build_extent("build_bvh", points)
-    data = dict(_C.build_bvh_batched_cooperative(points.unsqueeze(0)))
-    data.pop("batch_size")
-    for key in ("node_aabbs", "sorted_indices", "scene_min", "scene_max"):
-        data[key] = data[key].squeeze(0)
-    return BVHHandle(data)
+    return points
+
+
+def _build_bvh_single(points: torch.Tensor) -> BVHHandle:
+    points = _checked_build_points(_SINGLE, points)
+    payload = _C.build_bvh_batched_cooperative(points.unsqueeze(0))
+    # One cloud is a batch of one: drop the batch dimension of the per-cloud fields.
+    fields = {key: (value[0] if key in ("node_aabbs", "sorted_indices", "scene_min", "scene_max") else value)
+              for key, value in payload.items() if key != "batch_size"}
+    return BVHHandle(fields)
 
 
 def _build_bvh_batched(points: torch.Tensor) -> BatchedBVHHandle:
-    if points.dim() != 3:
-        raise ValueError("build_bvh: batched points must have shape (B, N, D)")
-    if points.size(2) not in SUPPORTED_DIMS:
-        raise ValueError("build_bvh: D must be 2 or 3")
-    _validate_cuda_float32("build_bvh", points, "points")
-    points = _as_contiguous(points)
-    _validate_narrow_build_extent("build_bvh", points)
-    return BatchedBVHHandle(_C.build_bvh_batched_cooperative(points))
+    return BatchedBVHHandle(_C.build_bvh_batched_cooperative(_checked_build_points(_BATCHED, points)))
 
 
 def _sample_payload(packed: Mapping, batch: int) -> dict:
-    """Per-sample BVHHandle payload as views into the packed ragged build."""
+    """Per-sample handle payload: views of the packed ragged build."""
     p0, p1 = packed["point_offsets"][batch], packed["point_offsets"][batch + 1]
     r0, r1 = packed["row_offsets"][batch], packed["row_offsets"][batch + 1]
-    n = p1 - p0
-    leaf_level = (n - 1).bit_length()
-    return {
-        "node_aabbs": packed["node_aabbs"][r0:r1],
-        "sorted_indices": packed["sorted_indices"][p0:p1],
-        "scene_min": packed["scene_min"][batch],
-        "scene_max": packed["scene_max"][batch],
-        "num_leaves": n,
-        "num_real_nodes": r1 - r0,
-        "leaf_level": leaf_level,
-        "virtual_leaves": (1 << leaf_level) - n,
-        "dim": packed["dim"],
-        "left_child_mem": packed["left_child_mem"][r0:r1],
-        "right_child_mem": packed["right_child_mem"][r0:r1],
-        "mem_to_leaf": packed["mem_to_leaf"][r0:r1],
-    }
+    fields = _C.tree_scalars(p1 - p0)
+    fields.update(
+        node_aabbs=packed["node_aabbs"][r0:r1],
+        sorted_indices=packed["sorted_indices"][p0:p1],
+        scene_min=packed["scene_min"][batch],
+        scene_max=packed["scene_max"][batch],
+        dim=packed["dim"],
+    )
+    fields.update(_C.deferred_traversal_arrays(p1 - p0, packed["node_aabbs"].device))
+    return fields
 
 
 def _build_bvh_ragged(points: torch.Tensor, batch_offsets: torch.Tensor) -> RaggedBVHHandle:
@@ -102,20 +171,16 @@ def _build_bvh_ragged(points: torch.Tensor, batch_offsets: torch.Tensor) -> Ragg
     batch_offsets = _as_contiguous_int64(batch_offsets)
     offsets = _validate_ragged_points("build_bvh", points, batch_offsets)
     packed = dict(_C.build_bvh_ragged(points, batch_offsets, offsets))
-    # The handle owns its own copy of the offsets, like the reference's handle payload.
+    # The handle keeps its own copy of the offsets.
     packed["point_offsets_device"] = batch_offsets.clone()
-    handles = [_LazyBVHHandle(lambda b=b: _sample_payload(packed, b)) for b in range(len(offsets) - 1)]
-    counts = torch.diff(batch_offsets).clone()
-    return RaggedBVHHandle(
-        {
-            "batch_offsets": packed["point_offsets_device"],
-            "num_leaves_per_sample": counts,
-            "batch_size": len(offsets) - 1,
-            "dim": int(points.size(1)),
-        },
-        handles,
-        packed,
-    )
+    samples = [_LazyBVHHandle(lambda b=b: _sample_payload(packed, b)) for b in range(len(offsets) - 1)]
+    meta = {
+        "batch_offsets": packed["point_offsets_device"],
+        "num_leaves_per_sample": torch.diff(batch_offsets),
+        "batch_size": len(offsets) - 1,
+        "dim": int(points.size(1)),
+    }
+    return RaggedBVHHandle(meta, samples, packed)
 
 
 def build_bvh(
@@ -132,82 +197,134 @@ def build_bvh(
     Ragged neighbor indices are local to each sample.
     """
     if batch_offsets is not None:
-        if points.dim() != 2:
-            raise ValueError("build_bvh: ragged mode requires 2-D points (total_N, D)")
+        _reject_unless(points.dim() == 2, "build_bvh: ragged mode requires 2-D points (total_N, D)")
         return _build_bvh_ragged(points, batch_offsets)
-    if points.dim() == 3:
-        return _build_bvh_batched(points)
-    if points.dim() == 2:
-        return _build_bvh_single(points)
-    raise ValueError("build_bvh: points must have shape (N, D) or (B, N, D)")
+    builders = {2: _build_bvh_single, 3: _build_bvh_batched}
+    _reject_unless(points.dim() in builders, "build_bvh: points must have shape (N, D) or (B, N, D)")
+    return builders[points.dim()](points)
 
 
 # ---------------------------------------------------------------------------
 # Queries
 # ---------------------------------------------------------------------------
 
-def _query_knn_single(
-    bvh: BVHHandle,
+def _checked_queries(layout: str, data: Mapping, query_points: torch.Tensor, device: torch.device) -> torch.Tensor:
+    for holds, text in _QUERY_SHAPE_RULES[layout]:
+        _reject_unless(holds(query_points, data), text)
+    _validate_cuda_float32("query_knn", query_points, "query_points")
+    _reject_unless(query_points.device == device, "query_knn: query_points must be on the same device as the BVH")
+    return _as_contiguous(query_points)
+
+
+def _run_fixed_size(data: Mapping, queries: torch.Tensor, k: int, source: torch.Tensor | None, sort_queries: bool,
+                    squeeze: bool):
+    """Single clouds (as B = 1) and fixed-size batches: Morton order of the
+    queries against each cloud's scene box, then the traversal."""
+    lift = (lambda t: t.unsqueeze(0)) if squeeze else (lambda t: t)
+    queries_b = lift(queries)
+    tree = (lift(data["node_aabbs"]), lift(data["sorted_indices"]))
+    sizes = (data["num_leaves"], data["num_real_nodes"], data["dim"], k)
+    order = None
+    if sort_queries:
+        order = _C.morton_sort_queries_narrow(queries_b, lift(data["scene_min"]), lift(data["scene_max"])).contiguous()
+    if source is not None:
+        idx, dist, pos = _C.query_knn_gather_positions(*tree, queries_b, order, lift(source.detach()), *sizes)
+        n = int(data["num_leaves"])
+        base = None if squeeze else (torch.arange(idx.size(0), device=idx.device, dtype=torch.int64) * n).view(-1, 1, 1)
+        if squeeze:
+            idx, dist, pos = idx[0], dist[0], pos[0]
+        return idx, dist, _with_source_grad(source, pos, idx, n, base)
+    if sort_queries:
+        idx, dist = _C.query_knn_batched_cached_bounds_ordered(*tree, queries_b, order, *sizes)
+    else:
+        idx, dist = _C.query_knn_batched_cached_bounds(*tree, queries_b, *sizes)
+    return (idx[0], dist[0]) if squeeze else (idx, dist)
+
+
+def _query_knn_single(bvh: BVHHandle, query_points: torch.Tensor, k: int, *,
+                      source_points: torch.Tensor | None = None, sort_queries: bool = True):
+    _validate_supported_k("query_knn", k)
+    data = _bvh_data(bvh, "query_knn")
+    queries = _checked_queries(_SINGLE, data, query_points, data["sorted_indices"].device)
+    if source_points is not None:
+        source_points = _check_source_points(_SINGLE, "query_knn", source_points, data["num_leaves"], None,
+                                             data["dim"], data["sorted_indices"].device)
+    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=True)
+
+
+def _query_knn_batched(bvh: BatchedBVHHandle, query_points: torch.Tensor, k: int, *,
+                       source_points: torch.Tensor | None = None, sort_queries: bool = True):
+    _validate_supported_k("query_knn", k)
+    data = _batched_bvh_data(bvh, "query_knn")
+    queries = _checked_queries(_BATCHED, data, query_points, data["sorted_indices"].device)
+    if source_points is not None:
+        source_points = _check_source_points(_BATCHED, "query_knn", source_points, data["num_leaves"],
+                                             data["batch_size"], data["dim"], data["sorted_indices"].device)
+    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=False)
+
+
+def _query_knn_ragged(bvh: RaggedBVHHandle, query_points: torch.Tensor, query_offsets: torch.Tensor, k: int, *,
+                      source_points: torch.Tensor | None = None):
+    _validate_supported_k("query_knn", k)
+    data, packed = _ragged_bvh_data(bvh, "query_knn")
+    device = data["batch_offsets"].device
+    queries = _checked_queries(_RAGGED, data, query_points, device)
+    query_offsets = _as_contiguous_int64(query_offsets)
+    q_offsets = _validate_offsets("query_knn", query_offsets, total_rows=int(queries.size(0)), device=queries.device)
+    _reject_unless(len(q_offsets) - 1 == data["batch_size"],
+                   "query_knn: query_offsets batch size must match BVH batch_size")
+    p_offsets = packed["point_offsets"]
+    _reject_unless(all(b - a >= k for a, b in zip(p_offsets, p_offsets[1:])),
+                   "query_knn: each source sample must contain at least k points")
+    if source_points is not None:
+        source_points = _check_source_points(_RAGGED, "query_knn", source_points, p_offsets[-1], None, data["dim"],
+                                             device)
+    total = q_offsets[-1]
+    order = _C.morton_sort_queries_ragged(queries, query_offsets, total, packed["scene_min"], packed["scene_max"])
+    if source_points is None:
+        return _C.query_knn_ragged(packed, queries, query_offsets, total, order, k)
+    idx, dist, pos = _C.query_knn_ragged(packed, queries, query_offsets, total, order, k,
+                                         source_points=source_points.detach())
+    if torch.is_grad_enabled() and source_points.requires_grad:
+        # Each query row's cloud: its first source row and its point count.
+        per_query = torch.diff(query_offsets)
+        starts = packed["point_offsets_device"]
+        row_base = torch.repeat_interleave(starts[:-1], per_query, output_size=total)[:, None]
+        sizes = torch.repeat_interleave(torch.diff(starts), per_query, output_size=total)[:, None]
+        pos = _with_source_grad(source_points, pos, idx, sizes, row_base)
+    return idx, dist, pos
+
+
+def query_knn(
+    bvh: BVHHandle | BatchedBVHHandle | RaggedBVHHandle,
     query_points: torch.Tensor,
     k: int,
     *,
+    query_offsets: torch.Tensor | None = None,
     source_points: torch.Tensor | None = None,
     sort_queries: bool = True,
 ):
-    _validate_supported_k("query_knn", k)
-    data = _bvh_data(bvh, "query_knn")
-    if query_points.dim() != 2:
-        raise ValueError("query_knn: query_points must have shape (M, D)")
-    if query_points.size(1) != data["dim"]:
-        raise ValueError("query_knn: query_points second dimension must match BVH dim")
-    _validate_cuda_float32("query_knn", query_points, "query_points")
-    if query_points.device != data["sorted_indices"].device:
-        raise ValueError("query_knn: query_points must be on the same device as the BVH")
-    query_points = _as_contiguous(query_points)
-    if source_points is not None:
-        _validate_single_source_points("query_knn", data, source_points)
-        source_points = _as_contiguous(source_points)
-    batched_queries = query_points.unsqueeze(0)
-    node_aabbs = data["node_aabbs"].unsqueeze(0)
-    sorted_indices = data["sorted_indices"].unsqueeze(0)
-    sort_perm = None
-    if sort_queries:
-        sort_perm = _C.morton_sort_queries_narrow(
-            batched_queries,
-            data["scene_min"].unsqueeze(0),
-            data["scene_max"].unsqueeze(0),
-        ).contiguous()
-    if source_points is not None:
-        indices, squared_distances, positions = _C.query_knn_gather_positions(
-            node_aabbs, sorted_indices, batched_queries, sort_perm, source_points.detach().unsqueeze(0),
-            data["num_leaves"], data["num_real_nodes"], data["dim"], k,
-        )
-        indices = indices.squeeze(0)
-        positions = _with_source_grad(source_points, positions.squeeze(0), indices, int(data["num_leaves"]))
-        return indices, squared_distances.squeeze(0), positions
-    if sort_queries:
-        indices, squared_distances = _C.query_knn_batched_cached_bounds_ordered(
-            node_aabbs,
-            sorted_indices,
-            batched_queries,
-            sort_perm,
-            data["num_leaves"],
-            data["num_real_nodes"],
-            data["dim"],
-            k,
-        )
-    else:
-        indices, squared_distances = _C.query_knn_batched_cached_bounds(
-            node_aabbs,
-            sorted_indices,
-            batched_queries,
-            data["num_leaves"],
-            data["num_real_nodes"],
-            data["dim"],
-            k,
-        )
-    return indices.squeeze(0), squared_distances.squeeze(0)
+    """Query exact k-NN. Dispatches on handle type.
 
+    - ``BVHHandle`` -> single-sample, returns shape ``(M, k)``
+    - ``BatchedBVHHandle`` -> batched, returns shape ``(B, M, k)``
+    - ``RaggedBVHHandle`` -> packed ragged; ``query_offsets`` required, returns packed ``(total_M, k)``
+
+    Returns ``(indices, squared_distances)`` or, when ``source_points`` is provided,
+    ``(indices, squared_distances, neighbor_positions)``.
+    """
+    if isinstance(bvh, RaggedBVHHandle):
+        _reject_unless(query_offsets is not None, "query_knn: query_offsets is required when querying a ragged BVH")
+        return _query_knn_ragged(bvh, query_points, query_offsets, k, source_points=source_points)
+    if query_offsets is not None:
+        raise TypeError("query_knn: query_offsets requires a RaggedBVHHandle")
+    run = _query_knn_batched if isinstance(bvh, BatchedBVHHandle) else _query_knn_single
+    return run(bvh, query_points, k, source_points=source_points, sort_queries=sort_queries)
+
+
+# ---------------------------------------------------------------------------
+# Differentiable neighbour positions from the fused gather
+# ---------------------------------------------------------------------------
 
 class _GatheredPositions(torch.autograd.Function):
     """Neighbour positions gathered inside the k-NN kernel, differentiable with
@@ -254,198 +371,3 @@ def _with_source_grad(source_points, positions, indices, cloud_size, row_base=No
     if row_base is not None:
         rows = rows + row_base
     return _GatheredPositions.apply(source_points, positions, rows)
-
-
-def _validate_single_source_points(prefix: str, data: Mapping, source_points: torch.Tensor) -> None:
-    if source_points.dim() != 2:
-        raise ValueError(f"{prefix}: source_points must have shape (N, D)")
-    if source_points.size(0) != data["num_leaves"]:
-        raise ValueError(f"{prefix}: source_points first dimension must match BVH num_leaves")
-    if source_points.size(1) != data["dim"]:
-        raise ValueError(f"{prefix}: source_points second dimension must match BVH dim")
-    _validate_cuda_float32(prefix, source_points, "source_points")
-    if source_points.device != data["sorted_indices"].device:
-        raise ValueError(f"{prefix}: source_points must be on the same device as the BVH")
-
-
-def _validate_batched_source_points(prefix: str, data: Mapping, source_points: torch.Tensor) -> None:
-    if source_points.dim() != 3:
-        raise ValueError(f"{prefix}: source_points must have shape (B, N, D)")
-    if source_points.size(0) != data["batch_size"]:
-        raise ValueError(f"{prefix}: source_points batch size must match BVH batch_size")
-    if source_points.size(1) != data["num_leaves"]:
-        raise ValueError(f"{prefix}: source_points second dimension must match BVH num_leaves")
-    if source_points.size(2) != data["dim"]:
-        raise ValueError(f"{prefix}: source_points last dimension must match BVH dim")
-    _validate_cuda_float32(prefix, source_points, "source_points")
-    if source_points.device != data["sorted_indices"].device:
-        raise ValueError(f"{prefix}: source_points must be on the same device as the BVH")
-
-
-def _query_knn_batched(
-    bvh: BatchedBVHHandle,
-    query_points: torch.Tensor,
-    k: int,
-    *,
-    source_points: torch.Tensor | None = None,
-    sort_queries: bool = True,
-):
-    _validate_supported_k("query_knn", k)
-    data = _batched_bvh_data(bvh, "query_knn")
-    if query_points.dim() != 3:
-        raise ValueError("query_knn: batched query_points must have shape (B, M, D)")
-    if query_points.size(0) != data["batch_size"]:
-        raise ValueError("query_knn: query_points batch size must match BVH batch_size")
-    if query_points.size(2) != data["dim"]:
-        raise ValueError("query_knn: query_points last dimension must match BVH dim")
-    _validate_cuda_float32("query_knn", query_points, "query_points")
-    if query_points.device != data["sorted_indices"].device:
-        raise ValueError("query_knn: query_points must be on the same device as the BVH")
-    query_points = _as_contiguous(query_points)
-    if source_points is not None:
-        _validate_batched_source_points("query_knn", data, source_points)
-        source_points = _as_contiguous(source_points)
-
-    sort_perm = None
-    if sort_queries:
-        sort_perm = _C.morton_sort_queries_narrow(query_points, data["scene_min"], data["scene_max"]).contiguous()
-    if source_points is not None:
-        indices, squared_distances, positions = _C.query_knn_gather_positions(
-            data["node_aabbs"], data["sorted_indices"], query_points, sort_perm, source_points.detach(),
-            data["num_leaves"], data["num_real_nodes"], data["dim"], k,
-        )
-        n = int(data["num_leaves"])
-        cloud_base = (torch.arange(indices.size(0), device=indices.device, dtype=torch.int64) * n).view(-1, 1, 1)
-        positions = _with_source_grad(source_points, positions, indices, n, cloud_base)
-        return indices, squared_distances, positions
-    if sort_queries:
-        indices, squared_distances = _C.query_knn_batched_cached_bounds_ordered(
-            data["node_aabbs"],
-            data["sorted_indices"],
-            query_points,
-            sort_perm,
-            data["num_leaves"],
-            data["num_real_nodes"],
-            data["dim"],
-            k,
-        )
-    else:
-        indices, squared_distances = _C.query_knn_batched_cached_bounds(
-            data["node_aabbs"],
-            data["sorted_indices"],
-            query_points,
-            data["num_leaves"],
-            data["num_real_nodes"],
-            data["dim"],
-            k,
-        )
-    return indices, squared_distances
-
-
-def _validate_ragged_source_points(
-    prefix: str,
-    data: Mapping,
-    source_points: torch.Tensor,
-    *,
-    total_rows: int,
-    device: torch.device,
-) -> None:
-    if source_points.dim() != 2:
-        raise ValueError(f"{prefix}: ragged source_points must have shape (total_N, D)")
-    if source_points.size(0) != total_rows:
-        raise ValueError(f"{prefix}: source_points first dimension must match BVH total_N")
-    if source_points.size(1) != data["dim"]:
-        raise ValueError(f"{prefix}: source_points second dimension must match BVH dim")
-    _validate_cuda_float32(prefix, source_points, "source_points")
-    if source_points.device != device:
-        raise ValueError(f"{prefix}: source_points must be on the same device as the BVH")
-
-
-def _query_knn_ragged(
-    bvh: RaggedBVHHandle,
-    query_points: torch.Tensor,
-    query_offsets: torch.Tensor,
-    k: int,
-    *,
-    source_points: torch.Tensor | None = None,
-):
-    _validate_supported_k("query_knn", k)
-
-    data, packed = _ragged_bvh_data(bvh, "query_knn")
-    if query_points.dim() != 2:
-        raise ValueError("query_knn: ragged query_points must have shape (total_M, D)")
-    if query_points.size(1) != data["dim"]:
-        raise ValueError("query_knn: query_points second dimension must match BVH dim")
-    _validate_cuda_float32("query_knn", query_points, "query_points")
-    if query_points.device != data["batch_offsets"].device:
-        raise ValueError("query_knn: query_points must be on the same device as the BVH")
-    query_points = _as_contiguous(query_points)
-    query_offsets = _as_contiguous_int64(query_offsets)
-
-    q_offsets = _validate_offsets(
-        "query_knn",
-        query_offsets,
-        total_rows=int(query_points.size(0)),
-        device=query_points.device,
-    )
-    if len(q_offsets) - 1 != data["batch_size"]:
-        raise ValueError("query_knn: query_offsets batch size must match BVH batch_size")
-
-    batch_offsets = packed["point_offsets"]
-    counts = [right - left for left, right in zip(batch_offsets, batch_offsets[1:])]
-    if any(count < k for count in counts):
-        raise ValueError("query_knn: each source sample must contain at least k points")
-
-    if source_points is not None:
-        _validate_ragged_source_points(
-            "query_knn",
-            data,
-            source_points,
-            total_rows=batch_offsets[-1],
-            device=query_points.device,
-        )
-        source_points = _as_contiguous(source_points)
-
-    total = q_offsets[-1]
-    order = _C.morton_sort_queries_ragged(query_points, query_offsets, total, packed["scene_min"], packed["scene_max"])
-    if source_points is None:
-        return _C.query_knn_ragged(packed, query_points, query_offsets, total, order, k)
-    indices, distances, positions = _C.query_knn_ragged(
-        packed, query_points, query_offsets, total, order, k, source_points=source_points.detach()
-    )
-    if torch.is_grad_enabled() and source_points.requires_grad:
-        query_counts = torch.diff(query_offsets)
-        point_offsets = packed["point_offsets_device"]
-        row_base = torch.repeat_interleave(point_offsets[:-1], query_counts, output_size=total)[:, None]
-        sizes = torch.repeat_interleave(torch.diff(point_offsets), query_counts, output_size=total)[:, None]
-        positions = _with_source_grad(source_points, positions, indices, sizes, row_base)
-    return indices, distances, positions
-
-
-def query_knn(
-    bvh: BVHHandle | BatchedBVHHandle | RaggedBVHHandle,
-    query_points: torch.Tensor,
-    k: int,
-    *,
-    query_offsets: torch.Tensor | None = None,
-    source_points: torch.Tensor | None = None,
-    sort_queries: bool = True,
-):
-    """Query exact k-NN. Dispatches on handle type.
-
-    - ``BVHHandle`` -> single-sample, returns shape ``(M, k)``
-    - ``BatchedBVHHandle`` -> batched, returns shape ``(B, M, k)``
-    - ``RaggedBVHHandle`` -> packed ragged; ``query_offsets`` required, returns packed ``(total_M, k)``
-
-    Returns ``(indices, squared_distances)`` or, when ``source_points`` is provided,
-    ``(indices, squared_distances, neighbor_positions)``.
-    """
-    if isinstance(bvh, RaggedBVHHandle):
-        if query_offsets is None:
-            raise ValueError("query_knn: query_offsets is required when querying a ragged BVH")
-        return _query_knn_ragged(bvh, query_points, query_offsets, k, source_points=source_points)
-    if query_offsets is not None:
-        raise TypeError("query_knn: query_offsets requires a RaggedBVHHandle")
-    if isinstance(bvh, BatchedBVHHandle):
-        return _query_knn_batched(bvh, query_points, k, source_points=source_points, sort_queries=sort_queries)
-    return _query_knn_single(bvh, query_points, k, source_points=source_points, sort_queries=sort_queries)

@@ -1,4 +1,13 @@
-"""Input validation with the reference's messages (torchbvh/_validation.py:6-75)."""
+"""Argument checks of the public calls.
+
+The exception types and message texts are part of the drop-in contract:
+``ValueError`` with the reference's wording (torchbvh/_validation.py:6-75),
+e.g. ``"build_bvh: points must be a CUDA tensor"``. Checks run in the
+reference's order, so an input with several problems reports the same one.
+
+Everything is phrased as small predicates over one tensor plus the message
+to raise, so each call site reads as the list of its rules.
+"""
 
 from __future__ import annotations
 
@@ -7,77 +16,58 @@ import torch
 from ._constants import SUPPORTED_DIMS, SUPPORTED_K
 
 
+def _reject_unless(ok: bool, message: str) -> None:
+    if not ok:
+        raise ValueError(message)
+
+
 def _validate_supported_k(prefix: str, k: int) -> None:
-    if k not in SUPPORTED_K:
-        # The reference message is kept verbatim as a prefix; k = 32 is this build's addition.
-        raise ValueError(f"{prefix}: k must be 4, 8, or 16 (or 32)")
+    # The reference's text stays a prefix of the message; k = 32 is this package's addition.
+    _reject_unless(k in SUPPORTED_K, f"{prefix}: k must be 4, 8, or 16 (or 32)")
 
 
 def _as_contiguous(tensor: torch.Tensor) -> torch.Tensor:
-    return tensor if tensor.is_contiguous() else tensor.contiguous()
+    return tensor.contiguous()
 
 
 def _as_contiguous_int64(tensor: torch.Tensor) -> torch.Tensor:
-    if tensor.dtype != torch.int64:
-        return tensor
-    return _as_contiguous(tensor)
+    # Only int64 offsets are made contiguous here; any other dtype is reported
+    # by the offsets check with its own message.
+    return tensor.contiguous() if tensor.dtype == torch.int64 else tensor
 
 
 def _validate_cuda_float32(prefix: str, tensor: torch.Tensor, name: str) -> None:
-    if not tensor.is_cuda:
-        raise ValueError(f"{prefix}: {name} must be a CUDA tensor")
-    if tensor.dtype != torch.float32:
-        raise ValueError(f"{prefix}: {name} must be float32")
-
-
-def _validate_cuda_float32_contiguous(prefix: str, tensor: torch.Tensor, name: str) -> None:
-    _validate_cuda_float32(prefix, tensor, name)
-    if not tensor.is_contiguous():
-        raise ValueError(f"{prefix}: {name} must be contiguous")
-
-
-def _validate_offsets(
-    prefix: str,
-    offsets: torch.Tensor,
-    *,
-    total_rows: int,
-    device: torch.device,
-) -> list[int]:
-    if offsets.dim() != 1:
-        raise ValueError(f"{prefix}: offsets must have shape (B + 1,)")
-    if offsets.numel() < 2:
-        raise ValueError(f"{prefix}: offsets must contain at least two entries")
-    if offsets.dtype != torch.int64:
-        raise ValueError(f"{prefix}: offsets must be int64")
-    if not offsets.is_cuda:
-        raise ValueError(f"{prefix}: offsets must be a CUDA tensor")
-    if not offsets.is_contiguous():
-        raise ValueError(f"{prefix}: offsets must be contiguous")
-    if offsets.device != device:
-        raise ValueError(f"{prefix}: offsets must be on the same device as the packed tensor")
-
-    values = [int(v) for v in offsets.detach().cpu().tolist()]
-    return _validate_offset_values(prefix, values, total_rows)
+    _reject_unless(tensor.is_cuda, f"{prefix}: {name} must be a CUDA tensor")
+    _reject_unless(tensor.dtype == torch.float32, f"{prefix}: {name} must be float32")
 
 
 def _validate_offset_values(prefix: str, values: list[int], total_rows: int) -> list[int]:
-    if values[0] != 0:
-        raise ValueError(f"{prefix}: offsets must start at 0")
-    if values[-1] != total_rows:
-        raise ValueError(f"{prefix}: final offset must match the packed tensor length")
-    if any(right <= left for left, right in zip(values, values[1:])):
-        raise ValueError(f"{prefix}: offsets must be strictly increasing")
+    """Host copy of an offsets vector: starts at 0, ends at the packed length, strictly increasing."""
+    _reject_unless(values[0] == 0, f"{prefix}: offsets must start at 0")
+    _reject_unless(values[-1] == total_rows, f"{prefix}: final offset must match the packed tensor length")
+    _reject_unless(all(b > a for a, b in zip(values, values[1:])), f"{prefix}: offsets must be strictly increasing")
     return values
 
 
-def _validate_ragged_points(
-    prefix: str,
-    points: torch.Tensor,
-    offsets: torch.Tensor,
-) -> list[int]:
-    if points.dim() != 2:
-        raise ValueError(f"{prefix}: points must have shape (total_N, D)")
-    if points.size(1) not in SUPPORTED_DIMS:
-        raise ValueError(f"{prefix}: D must be 2 or 3")
-    _validate_cuda_float32_contiguous(prefix, points, "points")
+def _validate_offsets(prefix: str, offsets: torch.Tensor, *, total_rows: int, device: torch.device) -> list[int]:
+    """Checks a (B + 1,) int64 CUDA offsets tensor and returns its host values."""
+    rules = (
+        (lambda: offsets.dim() == 1, "offsets must have shape (B + 1,)"),
+        (lambda: offsets.numel() >= 2, "offsets must contain at least two entries"),
+        (lambda: offsets.dtype == torch.int64, "offsets must be int64"),
+        (lambda: offsets.is_cuda, "offsets must be a CUDA tensor"),
+        (lambda: offsets.is_contiguous(), "offsets must be contiguous"),
+        (lambda: offsets.device == device, "offsets must be on the same device as the packed tensor"),
+    )
+    for holds, text in rules:
+        _reject_unless(holds(), f"{prefix}: {text}")
+    return _validate_offset_values(prefix, [int(v) for v in offsets.detach().cpu().tolist()], total_rows)
+
+
+def _validate_ragged_points(prefix: str, points: torch.Tensor, offsets: torch.Tensor) -> list[int]:
+    """Packed (total_N, D) CUDA float32 points plus their offsets; returns the host offsets."""
+    _reject_unless(points.dim() == 2, f"{prefix}: points must have shape (total_N, D)")
+    _reject_unless(points.size(1) in SUPPORTED_DIMS, f"{prefix}: D must be 2 or 3")
+    _validate_cuda_float32(prefix, points, "points")
+    _reject_unless(points.is_contiguous(), f"{prefix}: points must be contiguous")
     return _validate_offsets(prefix, offsets, total_rows=int(points.size(0)), device=points.device)

@@ -746,16 +746,20 @@ __global__ void __launch_bounds__(kTreeThreads) k_tree(TreeArgs a) {
     const int64_t first = g << delta;
     const int64_t group_end = (g + 1) << delta;
     const int64_t arrivals = (group_end < s_cnt[lv] ? group_end : s_cnt[lv]) - first;
-    __threadfence();
+    // The barrier orders every thread's row writes before thread 0's fence; the
+    // fence is cumulative, so one thread publishes the whole block's rows
+    // device-wide before taking the ticket (and, as the last arriver, orders
+    // the other blocks' rows before the merge below reads them).
     __syncthreads();
     if (tid == 0) {
+      __threadfence();
       const uint32_t old = atomicAdd(a.counters + t.counter + hop_base + g, 1u);
       if (int64_t(old) >= arrivals) device_error(a.status, kDevErrTreeCounter);
       s_last = int64_t(old) == arrivals - 1 ? 1 : 0;
+      __threadfence();
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     for (int m = lv - 1; m >= lam; --m) {
       const int64_t width = int64_t(1) << (m - lam);
       const int64_t jm = (g << (m - lam)) + tid;
@@ -769,12 +773,47 @@ __global__ void __launch_bounds__(kTreeThreads) k_tree(TreeArgs a) {
         }
         ctx.emit(m, jm, clo, chi);
       }
-      __threadfence();
-      __syncthreads();
+      __syncthreads();  // the next level reads these rows (same block)
     }
     hop_base += s_cnt[lam];
     lv = lam;
     j = g;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Traversal arrays of the implicit layout of one cloud (left/right child row,
+// leaf position), the values TreeCtx::emit writes. They depend only on the
+// point count, so a build may leave them out and a caller compute them when
+// they are first read.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_traversal_arrays(int64_t n, int L, int64_t rows, int32_t* left,
+                                                           int32_t* right, int32_t* m2l) {
+  __shared__ int64_t s_rowoff[34];
+  __shared__ int64_t s_cnt[34];
+  if (threadIdx.x <= unsigned(L)) s_cnt[threadIdx.x] = level_count(n, L, int(threadIdx.x));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t acc = 0;
+    for (int l = 0; l <= L; ++l) { s_rowoff[l] = acc; acc += s_cnt[l]; }
+    s_rowoff[L + 1] = acc;
+  }
+  __syncthreads();
+  for (int64_t row = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; row < rows;
+       row += int64_t(gridDim.x) * blockDim.x) {
+    int level = 0;
+    while (level < L && s_rowoff[level + 1] <= row) ++level;
+    const int64_t j = row - s_rowoff[level];
+    if (level == L) {
+      left[row] = -1;
+      right[row] = -1;
+      m2l[row] = int32_t(j);
+    } else {
+      const int64_t c0 = 2 * j;
+      left[row] = int32_t(s_rowoff[level + 1] + c0);
+      right[row] = c0 + 1 < s_cnt[level + 1] ? int32_t(s_rowoff[level + 1] + c0 + 1) : -1;
+      m2l[row] = -1;
+    }
   }
 }
 
@@ -783,6 +822,16 @@ __global__ void __launch_bounds__(kTreeThreads) k_tree(TreeArgs a) {
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
+cudaError_t launch_traversal_arrays(int64_t n, int32_t* left, int32_t* right, int32_t* m2l, cudaStream_t stream) {
+  const int L = ceil_log2_i64(n);
+  const int64_t rows = real_node_count(n);
+  int64_t grid = (rows + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  k_traversal_arrays<<<unsigned(grid), 256, 0, stream>>>(n, L, rows, left, right, m2l);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 SortPlan make_sort_plan(int64_t n, int num_clouds, int dim) {
   SortPlan p;
   p.n = n;

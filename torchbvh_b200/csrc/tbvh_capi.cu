@@ -216,6 +216,22 @@ int tbvh_build(int device, const float* points, int64_t num_clouds, int64_t poin
   return TBVH_OK;
 }
 
+int tbvh_traversal_arrays(int device, int64_t num_points, int32_t* left_child_mem, int32_t* right_child_mem,
+                          int32_t* mem_to_leaf, void* stream) {
+  const char* op = "build_traversal_arrays";
+  g_last_error.clear();
+  if (num_points < 1 || num_points > INT_MAX)
+    return fail(TBVH_ERR_BAD_ARG, "%s: point count must be in [1, 2^31)", op);
+  if (!left_child_mem || !right_child_mem || !mem_to_leaf)
+    return fail(TBVH_ERR_BAD_ARG, "%s: NULL output pointer", op);
+  int rc = set_device(device, op);
+  if (rc) return rc;
+  cudaError_t e = tbvh::launch_traversal_arrays(num_points, left_child_mem, right_child_mem, mem_to_leaf,
+                                                static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, op);
+  return TBVH_OK;
+}
+
 size_t tbvh_sort_queries_workspace_size(int64_t num_clouds, int64_t total_queries, int dim) {
   if (num_clouds < 1 || total_queries < 0 || (dim != 2 && dim != 3)) return 0;
   const tbvh::SortPlan p = tbvh::make_sort_plan(total_queries, int(num_clouds), dim);

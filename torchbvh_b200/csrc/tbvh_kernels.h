@@ -83,6 +83,9 @@ struct BuildLaunch {
 
 cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream);
 
+// left_child_mem / right_child_mem / mem_to_leaf of one cloud of n points.
+cudaError_t launch_traversal_arrays(int64_t n, int32_t* left, int32_t* right, int32_t* m2l, cudaStream_t stream);
+
 struct QuerySortLaunch {
   const float* queries;
   CloudMap clouds;

@@ -11,19 +11,23 @@
 //    its queries are spatial neighbours. The warp walks the implicit tree as a
 //    packet: a node is entered when any lane's lower bound admits it, child
 //    order is a lane majority vote, and the deferred-sibling stack keeps the
-//    node id once per warp plus one bound per lane in shared memory. Node box
-//    loads are warp-uniform (one transaction each).
+//    node id once per warp (plus, optionally, one bound per lane) in shared
+//    memory. Node box loads are warp-uniform (one transaction each).
 //  * The tree is cut 5 levels above the leaves: a node there covers <= 32
 //    consecutive sorted leaves ("bucket"), which the warp stages into shared
 //    memory with one coalesced load (coordinates + original index) and then
 //    scans with broadcast reads, every lane testing every point.
-//  * Each lane keeps its top-k sorted in registers as packed (distance bits,
-//    original index) keys, seeded from the sorted leaves around the query's
-//    own Morton rank before the traversal starts. Pruning keeps the reference's rule (skip a node only if
-//    its lower bound is strictly greater than the k-th distance), so the
-//    result is the exact k smallest (distance, index) pairs: identical to the
-//    reference except for the order among exactly tied distances, which the
-//    reference leaves unspecified (docs/algorithms.md, k-NN Query).
+//  * Each lane keeps its top-k as packed (distance bits, original index) keys,
+//    seeded from the sorted leaves around the query's own Morton rank before
+//    the traversal starts. For k <= 8 the keys are an ascending list in
+//    registers; for k >= 16 they are a per-lane max-heap in shared memory
+//    (one insertion is a sift-down of log2(k) levels instead of k selects,
+//    and the k keys leave the register file), heap-sorted in place at the end.
+//    Pruning keeps the reference's rule (skip a node only if its lower bound
+//    is strictly greater than the k-th distance), so the result is the exact k
+//    smallest (distance, index) pairs: identical to the reference except for
+//    the order among exactly tied distances, which the reference leaves
+//    unspecified (docs/algorithms.md, k-NN Query).
 //  * Queries of several clouds may share a warp (ragged batches); the warp
 //    serves each cloud in turn with the other lanes disabled.
 #include "tbvh_kernels.h"
@@ -44,6 +48,47 @@ constexpr int kBucketLevels = TBVH_KNN_BUCKET_LEVELS;  // bucket = 2^levels leav
 constexpr int kBucketSize = 1 << kBucketLevels;
 static_assert(kBucketSize <= 32, "a bucket is staged by one warp");
 constexpr int kStackDepth = 28;   // >= deepest bucket level + 1 for N < 2^31 (27)
+// Smallest k kept as a shared-memory heap (smaller k: register list).
+#ifndef TBVH_KNN_HEAP_MIN_K
+#define TBVH_KNN_HEAP_MIN_K 16
+#endif
+// 1: the stack keeps each lane's bound of a deferred node; 0: the bound is
+// recomputed from the node box when the node is popped (less shared memory).
+#ifndef TBVH_KNN_STACK_BOUNDS
+#define TBVH_KNN_STACK_BOUNDS 1
+#endif
+constexpr bool kStackBounds = TBVH_KNN_STACK_BOUNDS != 0;
+// Seeding window: this many times k sorted leaves around the query's rank.
+#ifndef TBVH_KNN_SEED_WINDOW
+#define TBVH_KNN_SEED_WINDOW 2
+#endif
+constexpr int kSeedWindow = TBVH_KNN_SEED_WINDOW;
+static_assert(kSeedWindow >= 1, "the window must hold at least k leaves");
+// Developer option: -DTBVH_KNN_PROFILE=1 sums, over warps, the clock cycles
+// of each traversal phase and counts of its events into g_knn_profile
+// (slots: 0 rank search, 1 seeding window, 2 node steps, 3 bucket load + marks,
+// 4 insertion rounds, 5 stack pops, 6 heap sort + row writes; 8 node steps,
+// 9 buckets, 10 insertion rounds, 11 insertions, 12 pops, 13 warp passes,
+// 14 active lanes). Off by default; timings taken with it on are not reported.
+#ifndef TBVH_KNN_PROFILE
+#define TBVH_KNN_PROFILE 0
+#endif
+#if TBVH_KNN_PROFILE
+__device__ unsigned long long g_knn_profile[16];
+#define KNN_PF_LAP(slot)                  \
+  do {                                    \
+    const long long now_ = clock64();     \
+    pf_[slot] += now_ - pf_t_;            \
+    pf_t_ = now_;                         \
+  } while (0)
+#define KNN_PF_CNT(slot, n) (pf_[slot] += (n))
+#else
+#define KNN_PF_LAP(slot) ((void)0)
+#define KNN_PF_CNT(slot, n) ((void)0)
+#endif
+
+template <int K>
+__host__ __device__ constexpr bool heap_topk() { return K >= TBVH_KNN_HEAP_MIN_K; }
 
 struct KnnArgs {
   const float* node_aabbs;
@@ -69,10 +114,12 @@ struct KnnArgs {
 
 using u64 = unsigned long long;
 
+template <int K>
 struct KnnSmem {
   float4 bucket[kKnnWarps][32];
-  float stack_dist[kKnnWarps][kStackDepth][32];
   uint32_t stack_node[kKnnWarps][kStackDepth];
+  float stack_dist[kStackBounds ? kKnnWarps : 1][kStackBounds ? kStackDepth : 1][32];
+  u64 heap[heap_topk<K>() ? kKnnWarps : 1][heap_topk<K>() ? K : 1][32];  // [warp][slot][lane]
 };
 
 // A top-k slot is one 64-bit key: distance bits above, source index below.
@@ -87,17 +134,122 @@ __device__ __forceinline__ float key_dist(u64 k) { return __uint_as_float(uint32
 __device__ __forceinline__ int32_t key_idx(u64 k) { return int32_t(uint32_t(k)); }
 constexpr u64 kEmptyKey = (u64(0x7f7fffffu) << 32) | u64(0xffffffffu);
 
-// Inserts nk (nk < key[K-1]) into the ascending list. Every slot decides its
-// new value from two independent comparisons, so there is no serial chain.
+// ---------------------------------------------------------------------------
+// Top-k containers. Both hold the K smallest keys offered so far; `kth` is the
+// largest of them (the acceptance threshold: a candidate enters only if its
+// key is strictly smaller).
+// ---------------------------------------------------------------------------
+
+// k <= 8: ascending list in registers. An insertion decides every slot from
+// two independent comparisons (no serial chain).
+template <int K, bool kHeap>
+struct TopK {
+  u64 key[K];
+  u64 kth;
+
+  __device__ __forceinline__ void init(u64* /*heap_lane*/) {
+#pragma unroll
+    for (int i = 0; i < K; ++i) key[i] = kEmptyKey;
+    kth = kEmptyKey;
+  }
+  // Fills the list from K keys given one at a time (any order), then sorts.
+  __device__ __forceinline__ void seed_slot(int i, u64 v) {
+#pragma unroll
+    for (int s = 0; s < K; ++s)
+      if (s == i) key[s] = v;
+  }
+  __device__ __forceinline__ void seed_done() {
+    sort();
+    kth = key[K - 1];
+  }
+  __device__ __forceinline__ void insert(u64 nk) {  // requires nk < kth
+    bool before[K];
+#pragma unroll
+    for (int s = 0; s < K; ++s) before[s] = nk < key[s];
+#pragma unroll
+    for (int s = K - 1; s > 0; --s) key[s] = before[s] ? (before[s - 1] ? key[s - 1] : nk) : key[s];
+    key[0] = before[0] ? nk : key[0];
+    kth = key[K - 1];
+  }
+  __device__ __forceinline__ void finish() {}
+  __device__ __forceinline__ u64 at(int i) const { return key[i]; }
+
+  // In-register bitonic sort, ascending.
+  __device__ __forceinline__ void sort() {
+#pragma unroll
+    for (int size = 2; size <= K; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+        for (int i = 0; i < K; ++i) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool ascending = (i & size) == 0;
+            const u64 a = key[i], b = key[j];
+            const bool swap = ascending ? b < a : a < b;
+            key[i] = swap ? b : a;
+            key[j] = swap ? a : b;
+          }
+        }
+      }
+    }
+  }
+};
+
+// k >= 16: max-heap per lane in shared memory, slot s of the lane at
+// h[s * 32] (consecutive lanes in consecutive words, so a warp's accesses to
+// any mix of slots are free of bank conflicts beyond the 64-bit split).
 template <int K>
-__device__ __forceinline__ void topk_insert(u64 (&key)[K], u64 nk) {
-  bool before[K];
-#pragma unroll
-  for (int s = 0; s < K; ++s) before[s] = nk < key[s];
-#pragma unroll
-  for (int s = K - 1; s > 0; --s) key[s] = before[s] ? (before[s - 1] ? key[s - 1] : nk) : key[s];
-  key[0] = before[0] ? nk : key[0];
-}
+struct TopK<K, true> {
+  u64* h;
+  u64 kth;  // the root, h[0]
+
+  __device__ __forceinline__ void init(u64* heap_lane) {
+    h = heap_lane;
+    kth = kEmptyKey;
+  }
+  // Moves x down from slot i of a heap of n slots.
+  __device__ __forceinline__ void sift_down(int i, u64 x, int n) {
+#pragma unroll 1
+    for (;;) {
+      int c = 2 * i + 1;
+      if (c >= n) break;
+      u64 a = h[c * 32];
+      if (c + 1 < n) {
+        const u64 b = h[(c + 1) * 32];
+        if (b > a) {
+          a = b;
+          ++c;
+        }
+      }
+      if (a <= x) break;
+      h[i * 32] = a;
+      i = c;
+    }
+    h[i * 32] = x;
+  }
+  __device__ __forceinline__ void seed_slot(int i, u64 v) { h[i * 32] = v; }
+  __device__ __forceinline__ void seed_done() {  // bottom-up heapify
+#pragma unroll 1
+    for (int i = K / 2 - 1; i >= 0; --i) sift_down(i, h[i * 32], K);
+    kth = h[0];
+  }
+  __device__ __forceinline__ void insert(u64 nk) {  // requires nk < kth: replaces the root
+    sift_down(0, nk, K);
+    kth = h[0];
+  }
+  // In-place heap sort: slots end ascending.
+  __device__ __forceinline__ void finish() {
+#pragma unroll 1
+    for (int end = K - 1; end > 0; --end) {
+      const u64 top = h[0];
+      const u64 last = h[end * 32];
+      h[end * 32] = top;
+      sift_down(0, last, end);
+    }
+  }
+  __device__ __forceinline__ u64 at(int i) const { return h[i * 32]; }
+};
 
 template <int D>
 __device__ __forceinline__ void load_box(const float* rows, int64_t row, float* lo, float* hi) {
@@ -115,28 +267,6 @@ __device__ __forceinline__ void load_box(const float* rows, int64_t row, float* 
   }
 }
 
-// In-register bitonic sort of the K keys, ascending.
-template <int K>
-__device__ __forceinline__ void topk_sort(u64 (&key)[K]) {
-#pragma unroll
-  for (int size = 2; size <= K; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-      for (int i = 0; i < K; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool ascending = (i & size) == 0;
-          const u64 a = key[i], b = key[j];
-          const bool swap = ascending ? b < a : a < b;
-          key[i] = swap ? b : a;
-          key[j] = swap ? a : b;
-        }
-      }
-    }
-  }
-}
-
 template <int D>
 __device__ __forceinline__ void load_leaf(const float* rows, int64_t row, float* p) {
   const float* r = rows + row * (2 * D);
@@ -146,9 +276,22 @@ __device__ __forceinline__ void load_leaf(const float* rows, int64_t row, float*
   if constexpr (D == 3) p[2] = __ldg(r + 2);
 }
 
+// Writes the K ascending keys as one result row, four slots at a time.
+template <int K, bool kHeap>
+__device__ __forceinline__ void write_row(const TopK<K, kHeap>& top, int64_t* oi, float* od) {
+#pragma unroll
+  for (int i = 0; i < K; i += 4) {
+    const u64 k0 = top.at(i), k1 = top.at(i + 1), k2 = top.at(i + 2), k3 = top.at(i + 3);
+    reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(k0), key_idx(k1));
+    reinterpret_cast<longlong2*>(oi)[i / 2 + 1] = make_longlong2(key_idx(k2), key_idx(k3));
+    reinterpret_cast<float4*>(od)[i / 4] = make_float4(key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
+  }
+}
+
 template <int D, int K, bool kToDest>
-__device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int cloud, bool mine, int64_t pos,
+__device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, int cloud, bool mine, int64_t pos,
                                              unsigned lane, unsigned warp) {
+  constexpr bool kHeap = heap_topk<K>();
   // Cloud facts.
   CloudTree t;
   if (a.table) {
@@ -165,6 +308,11 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   const int64_t q_off = a.qry.start(cloud);
   const float* rows = a.node_aabbs + t.row_off * (2 * D);
   const int64_t* sorted = a.sorted + pt_off;
+#if TBVH_KNN_PROFILE
+  unsigned long long pf_[16] = {};
+  long long pf_t_ = clock64();
+  const int pf_leader = __ffs(__ballot_sync(kFullMask, mine)) - 1;
+#endif
 
   // Lane l holds cnt(l) and rowoff(l) of level l (l <= L <= 31).
   const int64_t my_cnt = int(lane) <= L ? level_count(n, L, int(lane)) : 0;
@@ -197,18 +345,14 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
     for (int c = 0; c < D; ++c) q[c] = a.queries[gq * D + c];
   }
 
-  u64 key[K];
-#pragma unroll
-  for (int i = 0; i < K; ++i) key[i] = kEmptyKey;
-
+  TopK<K, kHeap> top;
+  top.init(kHeap ? &s.heap[kHeap ? warp : 0][0][lane] : nullptr);
   float kth = mine ? kFar : -1.0f;  // disabled lanes admit nothing
-  u64 kth_key = mine ? kEmptyKey : 0ull;
   // Offers a candidate key whose distance is already known to be < FLT_MAX.
   auto offer = [&](u64 nk) {
-    if (nk < kth_key) {
-      topk_insert<K>(key, nk);
-      kth_key = key[K - 1];
-      kth = key_dist(kth_key);
+    if (nk < top.kth) {
+      top.insert(nk);
+      kth = key_dist(top.kth);
     }
   };
 
@@ -218,7 +362,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
   // in Morton order, so this makes the k-th distance tight before the exact
   // traversal starts; that traversal then skips the seeded window per lane.
   // The window only affects speed: every seeded point is fully evaluated.
-  const int64_t win = n < int64_t(2 * K) ? n : int64_t(2 * K);
+  const int64_t win = n < int64_t(kSeedWindow * K) ? n : int64_t(kSeedWindow * K);
   int64_t w0 = 0;
   if (mine) {
     const uint32_t qcode = morton_code<D>(q, root_lo, root_hi);
@@ -229,28 +373,27 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
       load_leaf<D>(rows, leaf_row0 + mid, p);
       if (morton_code<D>(p, root_lo, root_hi) < qcode) lo = mid + 1; else hi = mid;
     }
-    w0 = lo - K;
+    w0 = lo - win / 2;
     if (w0 > n - win) w0 = n - win;
     if (w0 < 0) w0 = 0;
   }
+  KNN_PF_LAP(0);
   const int64_t w1 = mine ? w0 + win : 0;
   // The first K window points fill the list (only distances < FLT_MAX enter,
-  // as with insertions into an empty list), then one bitonic sort.
+  // as with insertions into an empty list), then the rest are offered.
+  if (mine) {
 #pragma unroll
-  for (int i = 0; i < K; ++i) {
-    if (mine) {
+    for (int i = 0; i < K; ++i) {
       float p[D];
       load_leaf<D>(rows, leaf_row0 + w0 + i, p);
       const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      key[i] = d < kFar ? pack_key(d, int32_t(sorted[w0 + i])) : kEmptyKey;
+      top.seed_slot(i, d < kFar ? pack_key(d, int32_t(sorted[w0 + i])) : kEmptyKey);
     }
+    top.seed_done();
+    kth = key_dist(top.kth);
+  } else {
+    top.kth = 0ull;  // accepts nothing
   }
-  topk_sort<K>(key);
-  if (mine) {
-    kth_key = key[K - 1];
-    kth = key_dist(kth_key);
-  }
-  // The rest of the window.
   for (int64_t i = K; i < win; ++i) {
     if (mine) {
       float p[D];
@@ -259,6 +402,8 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
       if (d < kFar) offer(pack_key(d, int32_t(sorted[w0 + i])));
     }
   }
+  __syncwarp();
+  KNN_PF_LAP(1);
 
   // ---- Exact packet traversal from the root.
   int level = 0;
@@ -302,18 +447,26 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
           const uint32_t upto = b1 >= 32 ? 0xffffffffu : ((1u << b1) - 1u);
           cand &= ~(upto & ~((1u << b0) - 1u));
         }
+        __syncwarp();
+        KNN_PF_LAP(3);
+        KNN_PF_CNT(9, 1);
         // Pass 2: insert the marked points, one per lane per round, so the warp
         // pays max-over-lanes(marks) insertions per bucket.
         while (__any_sync(kFullMask, cand != 0u)) {
+          KNN_PF_CNT(10, 1);
           if (cand) {
             const int i = __ffs(cand) - 1;
             cand &= cand - 1u;
             const float4 p = s.bucket[warp][i];
             const float d = point_dist2<D>(q, p.x, p.y, p.z);
+#if TBVH_KNN_PROFILE
+            if (d < kFar && pack_key(d, __float_as_int(p.w)) < top.kth) KNN_PF_CNT(11, 1);
+#endif
             if (d < kFar) offer(pack_key(d, __float_as_int(p.w)));
           }
         }
         __syncwarp();
+        KNN_PF_LAP(4);
       } else {
         const int cl = level + 1;
         const int64_t c0 = node * 2;
@@ -341,82 +494,101 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
         const int64_t far_j = left_first ? c0 + 1 : c0;
         if (__any_sync(kFullMask, far_d <= kth)) {
           if (sp < kStackDepth) {
-            s.stack_dist[warp][sp][lane] = far_d;
+            if constexpr (kStackBounds) s.stack_dist[warp][sp][lane] = far_d;
             if (lane == 0) s.stack_node[warp][sp] = uint32_t(far_j) | (uint32_t(cl) << 27);
             ++sp;
           } else if (lane == 0) {
             atomicOr(a.status, kDevErrStackOverflow);
           }
         }
+        KNN_PF_CNT(8, 1);
         if (__any_sync(kFullMask, near_d <= kth)) {
           level = cl;
           node = near_j;
           nd = near_d;
+          KNN_PF_LAP(2);
           continue;
         }
+        KNN_PF_LAP(2);
       }
       // Pop the next deferred node that some lane still needs (against the
       // lane's current k-th distance).
       bool found = false;
       while (sp > 0) {
         --sp;
+        KNN_PF_CNT(12, 1);
         __syncwarp();
         const uint32_t e = s.stack_node[warp][sp];
-        const float d = s.stack_dist[warp][sp][lane];
+        const int el = int(e >> 27);
+        const int64_t ej = int64_t(e & 0x07ffffffu);
+        float d;
+        if constexpr (kStackBounds) {
+          d = s.stack_dist[warp][sp][lane];
+        } else {
+          float lo[D], hi[D];
+          load_box<D>(rows, __shfl_sync(kFullMask, my_rowoff, el) + ej, lo, hi);
+          d = box_dist2<D>(q, lo, hi);
+        }
         if (__any_sync(kFullMask, d <= kth)) {
-          level = int(e >> 27);
-          node = int64_t(e & 0x07ffffffu);
+          level = el;
+          node = ej;
           nd = d;
           found = true;
           break;
         }
       }
+      KNN_PF_LAP(5);
       if (!found) break;
     }
   }
   (void)nd;
 
+#if TBVH_KNN_PROFILE
+  KNN_PF_CNT(13, 1);
+  KNN_PF_CNT(14, __popc(__ballot_sync(kFullMask, mine)));
+  if (mine) top.finish();
+  KNN_PF_LAP(6);
+  if (int(lane) == pf_leader) {
+    for (int i = 0; i < 16; ++i) atomicAdd(&g_knn_profile[i], pf_[i]);
+  }
+#endif
+  if (!mine) return;
+#if !TBVH_KNN_PROFILE
+  top.finish();
+#endif
   if constexpr (kToDest) {
-    if (!mine) return;
     // Result row delivered to every destination buffer at the query's row.
     // Destinations on other GPUs are written over NVLink as the results come
     // out of the traversal, so the exchange overlaps the remaining compute.
-    for (int dst = 0; dst < a.num_dest; ++dst) {
-      int64_t* oi = a.dest_idx[dst] + gq * K;
-      float* od = a.dest_dist[dst] + gq * K;
+    // Four slots at a time, each chunk to every destination, so only four keys
+    // are live in registers.
 #pragma unroll
-      for (int i = 0; i < K; i += 2) {
-        reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(key[i]), key_idx(key[i + 1]));
-      }
-#pragma unroll
-      for (int i = 0; i < K; i += 4) {
-        reinterpret_cast<float4*>(od)[i / 4] =
-            make_float4(key_dist(key[i]), key_dist(key[i + 1]), key_dist(key[i + 2]), key_dist(key[i + 3]));
+    for (int i = 0; i < K; i += 4) {
+      const u64 k0 = top.at(i), k1 = top.at(i + 1), k2 = top.at(i + 2), k3 = top.at(i + 3);
+      const longlong2 i01 = make_longlong2(key_idx(k0), key_idx(k1));
+      const longlong2 i23 = make_longlong2(key_idx(k2), key_idx(k3));
+      const float4 d4 = make_float4(key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
+#pragma unroll 1
+      for (int dst = 0; dst < a.num_dest; ++dst) {
+        longlong2* oi = reinterpret_cast<longlong2*>(a.dest_idx[dst] + gq * K + i);
+        oi[0] = i01;
+        oi[1] = i23;
+        *reinterpret_cast<float4*>(a.dest_dist[dst] + gq * K + i) = d4;
       }
     }
-  } else if (mine) {
+  } else {
     // Output row: the query's own row, or its position in the sorted order
     // (the reference's spatial variant, knn_query.cu:448-461).
     const int64_t row = a.spatial ? pos : gq;
-    int64_t* oi = a.out_idx + row * K;
-    float* od = a.out_dist + row * K;
-#pragma unroll
-    for (int i = 0; i < K; i += 2) {
-      reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(key[i]), key_idx(key[i + 1]));
-    }
-#pragma unroll
-    for (int i = 0; i < K; i += 4) {
-      reinterpret_cast<float4*>(od)[i / 4] =
-          make_float4(key_dist(key[i]), key_dist(key[i + 1]), key_dist(key[i + 2]), key_dist(key[i + 3]));
-    }
+    write_row<K, kHeap>(top, a.out_idx + row * K, a.out_dist + row * K);
     if (a.out_pos) {
       // Fused source_points[indices] gather. An empty slot (index -1) reads the
       // cloud's last point, as PyTorch's negative indexing would.
       const float* src = a.src_points + pt_off * D;
       float* op = a.out_pos + row * K * D;
-#pragma unroll
+#pragma unroll 4
       for (int i = 0; i < K; ++i) {
-        int64_t idx = key_idx(key[i]);
+        int64_t idx = key_idx(top.at(i));
         if (idx < 0) idx = n - 1;
 #pragma unroll
         for (int c = 0; c < D; ++c) op[i * D + c] = __ldg(src + idx * D + c);
@@ -428,7 +600,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem& s, int c
 template <int D, int K, bool kToDest>
 __global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
   extern __shared__ __align__(16) unsigned char knn_smem_raw[];
-  KnnSmem& s = *reinterpret_cast<KnnSmem*>(knn_smem_raw);
+  KnnSmem<K>& s = *reinterpret_cast<KnnSmem<K>*>(knn_smem_raw);
   const unsigned lane = threadIdx.x & 31u;
   const unsigned warp = threadIdx.x >> 5;
   const int64_t pos = (int64_t(blockIdx.x) * kKnnWarps + warp) * 32 + lane;
@@ -441,6 +613,7 @@ __global__ void __launch_bounds__(kKnnThreads) k_knn(KnnArgs a) {
     const bool mine = valid && cloud == cur;
     pending &= ~__ballot_sync(kFullMask, mine);
     search_cloud<D, K, kToDest>(a, s, cur, mine, pos, lane, warp);
+    __syncwarp();
   }
   // Peer stores must be visible system-wide before the kernel counts as done:
   // the caller's next collective tells the other GPUs that their rows arrived.
@@ -483,20 +656,35 @@ __global__ void __launch_bounds__(256) k_knn_table(CloudMap pts, CloudTree* tabl
   }
 }
 
+template <int D, int K, bool kToDest>
+cudaError_t launch_variant(const KnnArgs& a, unsigned blocks, cudaStream_t stream) {
+  constexpr size_t smem = sizeof(KnnSmem<K>);
+  static_assert(smem <= 227 * 1024, "traversal shared memory exceeds the per-block limit");
+  if constexpr (smem > 48 * 1024) {
+    // Opt in to more than the default 48 KB of dynamic shared memory. The
+    // attribute belongs to the device's context, so set it on every device once.
+    static bool set_on[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !set_on[dev]) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(k_knn<D, K, kToDest>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) set_on[dev] = true;
+    }
+  }
+  k_knn<D, K, kToDest><<<blocks, kKnnThreads, smem, stream>>>(a);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 template <int D, int K>
 cudaError_t launch_typed(const KnnArgs& a, cudaStream_t stream) {
   const int64_t warps = (a.total_q + 31) / 32;
   const int64_t blocks = (warps + kKnnWarps - 1) / kKnnWarps;
-  if (blocks > 0) {
-    static_assert(sizeof(KnnSmem) <= 48 * 1024, "fits the default dynamic shared memory limit");
-    if (a.num_dest > 0) {
-      k_knn<D, K, true><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
-    } else {
-      k_knn<D, K, false><<<unsigned(blocks), kKnnThreads, sizeof(KnnSmem), stream>>>(a);
-    }
-    count_launches(1);
-  }
-  return cudaGetLastError();
+  if (blocks <= 0) return cudaSuccess;
+  if (a.num_dest > 0) return launch_variant<D, K, true>(a, unsigned(blocks), stream);
+  return launch_variant<D, K, false>(a, unsigned(blocks), stream);
 }
 
 }  // namespace
