@@ -47,6 +47,18 @@ int tbvh_abi_version(void);
  * waits without bounds inside CUB). */
 int tbvh_device_status(int device, unsigned* out_bits, int clear);
 
+/* Self-test of the bounded device waits. No reference counterpart (the
+ * reference's sort waits inside CUB without a bound). Runs one radix-sort
+ * pass of this library over an internal key pattern in `workspace` whose
+ * tile 0 is never claimed, so tile 1's look-back wait must give up after a
+ * short bound (4,096 polls): the kernel records TBVH_DEVICE_LOOKBACK_TIMEOUT
+ * and returns, and the device stays usable. Synchronous on `stream`: clears
+ * the status word first, then stores the bits the pass raised in *out_bits
+ * (and clears them). workspace: tbvh_selftest_workspace_size() bytes. */
+size_t tbvh_selftest_workspace_size(void);
+int tbvh_selftest_lookback_timeout(int device, void* workspace, size_t workspace_bytes, void* stream,
+                                   unsigned* out_bits);
+
 /* Number of kernels this library has launched in this process (all devices).
  * Host-side counter; lets callers attribute launches to this library. */
 uint64_t tbvh_kernel_launch_count(void);

@@ -60,6 +60,8 @@ _SIGNATURES = {
         [_i32, _ptr, _i64, _i64, _ptr, _ptr, _i32, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i32, _ptr, _size, _ptr],
     ),
     "tbvh_traversal_arrays": (_i32, [_i32, _i64, _ptr, _ptr, _ptr, _ptr]),
+    "tbvh_selftest_workspace_size": (_size, []),
+    "tbvh_selftest_lookback_timeout": (_i32, [_i32, _ptr, _size, _ptr, ctypes.POINTER(ctypes.c_uint)]),
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),

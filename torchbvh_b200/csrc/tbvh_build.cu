@@ -353,6 +353,7 @@ struct PassArgs {
   int needs_cloud;
   CloudMap cm;
   unsigned* status;
+  int spin_limit;           // polls of one look-back wait before it gives up
 };
 
 struct PassSmem {
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_pass(PassArgs a) {
       const uint64_t v = lb[t * kRadix + d];
       const uint64_t flag = v & kLbFlags;
       if (flag == 0) {
-        if (++spins > kLbSpinLimit) {
+        if (++spins > a.spin_limit) {
           device_error(a.status, kDevErrLookbackTimeout);
           break;
         }
@@ -817,11 +818,60 @@ __global__ void __launch_bounds__(256) k_traversal_arrays(int64_t n, int L, int6
   }
 }
 
+// Self-test set-up: a key pattern and a ticket counter that starts at 1, so
+// no block of the following pass ever claims tile 0.
+__global__ void __launch_bounds__(256) k_selftest_prepare(uint32_t* keys, int64_t n, uint32_t* tile_ctr) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    keys[i] = uint32_t(i) * 2654435761u;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *tile_ctr = 1u;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
+constexpr int64_t kSelfTestElements = 4 * int64_t(kSortTile);
+
+size_t selftest_scratch_bytes() { return sort_scratch_bytes(make_sort_plan(kSelfTestElements, 1, 3)); }
+
+cudaError_t launch_lookback_selftest(void* scratch, int spin_limit, cudaStream_t stream) {
+  const SortPlan p = make_sort_plan(kSelfTestElements, 1, 3);
+  char* cur = static_cast<char*>(scratch);
+  SortScratch ss;
+  carve_sort_scratch(p, cur, ss);
+  InitArgs ia{};
+  ia.zero[0] = {ss.hist, int64_t(kMaxSortPasses) * kRadix};
+  ia.zero[2] = {reinterpret_cast<uint32_t*>(ss.lookback[0]), p.tiles * kRadix * 2};
+  k_init<<<8, 256, 0, stream>>>(ia);
+  k_selftest_prepare<<<16, 256, 0, stream>>>(ss.keys[0], p.n, ss.tile_ctr);
+  count_launches(2);
+  PassArgs a{};
+  a.keys_in = ss.keys[0];
+  a.vals_in = nullptr;
+  a.keys_out = ss.keys[1];
+  a.vals_out = ss.vals[1];
+  a.final_out = nullptr;
+  a.hist = ss.hist;
+  a.lookback = ss.lookback[0];
+  a.lookback_next = nullptr;
+  a.tile_ctr = ss.tile_ctr;
+  a.n = p.n;
+  a.lo_bit = 0;
+  a.code_bits = p.code_bits;
+  a.needs_cloud = 0;
+  a.cm.offsets = nullptr;
+  a.cm.uniform_n = p.n;
+  a.cm.num_clouds = 1;
+  a.status = device_status_ptr();
+  a.spin_limit = spin_limit;
+  // One block fewer than tiles: the blocks claim tickets 1 .. tiles-1, tile 0
+  // never publishes, and tile 1's wait on it must give up after spin_limit polls.
+  k_sort_pass<<<dim3(unsigned(p.tiles - 1)), kSortThreads, sizeof(PassSmem), stream>>>(a);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_traversal_arrays(int64_t n, int32_t* left, int32_t* right, int32_t* m2l, cudaStream_t stream) {
   const int L = ceil_log2_i64(n);
   const int64_t rows = real_node_count(n);
@@ -928,6 +978,7 @@ static cudaError_t run_sort_passes(const SortPlan& p, const SortScratch& ss, con
     a.needs_cloud = (8 * ps + 8 > p.code_bits && p.cloud_bits > 0) || (last && cm.num_clouds > 1) ? 1 : 0;
     a.cm = cm;
     a.status = status;
+    a.spin_limit = kLbSpinLimit;
     k_sort_pass<<<dim3(unsigned(p.tiles)), kSortThreads, smem, stream>>>(a);
     count_launches(1);
     src ^= 1;

@@ -146,6 +146,28 @@ int tbvh_device_status(int device, unsigned* out_bits, int clear) {
   return TBVH_OK;
 }
 
+size_t tbvh_selftest_workspace_size(void) { return tbvh::selftest_scratch_bytes(); }
+
+int tbvh_selftest_lookback_timeout(int device, void* workspace, size_t workspace_bytes, void* stream,
+                                   unsigned* out_bits) {
+  const char* op = "tbvh_selftest_lookback_timeout";
+  g_last_error.clear();
+  if (out_bits == nullptr) return fail(TBVH_ERR_BAD_ARG, "%s: out_bits is NULL", op);
+  if (workspace == nullptr || workspace_bytes < tbvh::selftest_scratch_bytes())
+    return fail(TBVH_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the required %zu", op,
+                workspace_bytes, tbvh::selftest_scratch_bytes());
+  int rc = set_device(device, op);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = tbvh::read_device_status(out_bits, true);  // start from a clear word
+  if (e == cudaSuccess) e = tbvh::launch_lookback_selftest(workspace, 1 << 12, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = tbvh::read_device_status(out_bits, true);
+  if (e != cudaSuccess) return cuda_fail(e, op);
+  return TBVH_OK;
+}
+
 int64_t tbvh_real_node_count(int64_t num_points) {
   return num_points > 0 ? tbvh::real_node_count(num_points) : 0;
 }

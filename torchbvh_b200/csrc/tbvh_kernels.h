@@ -83,6 +83,12 @@ struct BuildLaunch {
 
 cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream);
 
+// Bounded-wait self-test: one sort pass whose tile 0 is never claimed, so the
+// look-back wait of tile 1 gives up after spin_limit polls and raises
+// kDevErrLookbackTimeout. Scratch of selftest_scratch_bytes().
+size_t selftest_scratch_bytes();
+cudaError_t launch_lookback_selftest(void* scratch, int spin_limit, cudaStream_t stream);
+
 // left_child_mem / right_child_mem / mem_to_leaf of one cloud of n points.
 cudaError_t launch_traversal_arrays(int64_t n, int32_t* left, int32_t* right, int32_t* m2l, cudaStream_t stream);
 
