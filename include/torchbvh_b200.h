@@ -189,6 +189,22 @@ int tbvh_peer_free(int device, void* ptr);
 int tbvh_peer_open(int device, const void* handle, void** out_ptr);
 int tbvh_peer_close(int device, void* ptr);
 
+/* This rank's share of the num_queries queries of one cloud, in Morton order
+ * (codes against scene_min/scene_max, the BVH's scene box). No counterpart in
+ * the reference. The code range is cut at cells of its top 15 bits; walking
+ * the cells in code order, runs of about `chunk` queries go to ranks 0, 1, ..,
+ * world-1, 0, 1, .. (chunk = ceil(num_queries / world) gives each rank one
+ * contiguous Morton range; smaller chunks interleave the ranks over the
+ * cloud). Every rank computes the same split from the same inputs, so the
+ * shares of all ranks partition the queries with no exchange. Writes the
+ * share's query indices (int64, ascending Morton code) to share_out (capacity
+ * num_queries) and their number to *share_count (host). Synchronous on
+ * `stream` (the count is read back before the share is sorted). */
+size_t tbvh_share_queries_workspace_size(int64_t num_queries, int dim);
+int tbvh_share_queries(int device, const float* queries, int64_t num_queries, int dim, const float* scene_min,
+                       const float* scene_max, int rank, int world, int64_t chunk, int64_t* share_out,
+                       int64_t* share_count, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Exact k-NN of this rank's share of the queries of one cloud (the BVH of
  * num_points points built by tbvh_build), with every result row written into
  * each of the num_dest (<= 8) destination buffers at the query's own row:

@@ -6,6 +6,7 @@ destinations) is covered by tests/test_gpu_distributed.py.
 """
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -94,3 +95,55 @@ def test_peer_buffer_round_trip_on_one_device():
         assert int(t.sum()) == 1023 * 1024 // 2
     finally:
         _native.peer_free(0, ptr)
+
+
+@pytest.mark.parametrize("world,split", [(1, "morton"), (2, "morton"), (3, "morton"), (8, "morton"),
+                                         (4, "interleaved"), (8, "interleaved")])
+def test_query_shares_partition_the_queries_in_morton_order(oracle, world, split):
+    """tbvh_share_queries on one GPU, every rank's share in turn: the shares
+    partition the queries, each share is in ascending Morton order (codes against
+    the BVH's scene box), and the share sizes are balanced to the cell size."""
+    from torchbvh_b200 import distributed as tdist
+
+    g = torch.Generator().manual_seed(40 + world)
+    points = torch.rand((60_000, 3), generator=g).cuda()
+    queries = torch.rand((50_001, 3), generator=g).cuda()
+    m = queries.shape[0]
+    with torchbvh.BVH(points) as bvh:
+        h = bvh._handle
+        shares = [tdist._owned_queries_cuda(h, queries, r, world, split) for r in range(world)]
+        lo, hi = h["scene_min"].cpu().numpy(), h["scene_max"].cpu().numpy()
+    torch.cuda.synchronize()
+    allq = torch.cat(shares).cpu()
+    assert torch.equal(torch.sort(allq).values, torch.arange(m))
+    # The oracle's Morton codes divide with IEEE division where the kernels use
+    # the fast-math quotient, so a query within an ulp of a cell boundary may
+    # differ by one cell: allow a handful of inversions.
+    codes = oracle.morton_codes(queries.cpu().numpy(), lo, hi).astype(np.int64)
+    for s in shares:
+        c = codes[s.cpu().numpy()]
+        assert np.count_nonzero(np.diff(c) < 0) <= 4
+    sizes = [s.numel() for s in shares]
+    # A 15-bit cell of this uniform cloud holds about m / 32768 queries.
+    runs = 1 if split == "morton" else 32
+    assert max(sizes) - min(sizes) <= 2 * runs * (4 * m // 32768 + 8)
+    assert torchbvh.device_status() == 0
+
+
+def test_interleaved_share_matches_single_gpu_results():
+    points = _cloud(60, (40_000, 3))
+    queries = _cloud(61, (20_000, 3))
+    from torchbvh_b200 import distributed as tdist
+
+    with torchbvh.BVH(points) as bvh:
+        want_i, want_d = bvh.knn(queries, 16)
+        h = bvh._handle
+        di = torch.full((20_000, 16), -1, dtype=torch.int64, device="cuda")
+        dd = torch.full((20_000, 16), -1.0, device="cuda")
+        for r in range(4):
+            share = tdist._owned_queries_cuda(h, queries, r, 4, "interleaved")
+            _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 40_000, queries, share, 16,
+                                    [di.data_ptr()], [dd.data_ptr()])
+    torch.cuda.synchronize()
+    assert torch.equal(di, want_i) and torch.equal(dd, want_d)
+    assert torchbvh.device_status() == 0

@@ -65,6 +65,10 @@ _SIGNATURES = {
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),
+    "tbvh_share_queries_workspace_size": (_size, [_i64, _i32]),
+    "tbvh_share_queries": (
+        _i32, [_i32, _ptr, _i64, _i32, _ptr, _ptr, _i32, _i32, _i64, _ptr, ctypes.POINTER(_i64), _ptr, _size, _ptr],
+    ),
     "tbvh_peer_handle_bytes": (_size, []),
     "tbvh_peer_alloc": (_i32, [_i32, _size, ctypes.POINTER(_ptr), _ptr]),
     "tbvh_peer_free": (_i32, [_i32, _ptr]),
@@ -304,6 +308,24 @@ def morton_sort_queries_narrow(queries: torch.Tensor, scene_min: torch.Tensor, s
         scene_min.data_ptr(), scene_max.data_ptr(), order.data_ptr(), ws.data_ptr(), ws.numel(), _stream(device),
     ))
     return order
+
+
+def share_queries(queries: torch.Tensor, scene_min: torch.Tensor, scene_max: torch.Tensor, rank: int, world: int,
+                  chunk: int) -> torch.Tensor:
+    """This rank's share of the (M, D) queries of one cloud, as int64 query
+    indices in Morton order (see tbvh_share_queries). Synchronises the stream."""
+    if not (queries.is_cuda and queries.is_contiguous() and queries.dtype == torch.float32 and queries.dim() == 2):
+        raise RuntimeError("share_queries: queries must be contiguous CUDA float32 (M, D)")
+    m, dim = int(queries.size(0)), int(queries.size(1))
+    device = queries.device
+    lib = load_library()
+    out = torch.empty((m,), dtype=torch.int64, device=device)
+    ws = _workspace(lib.tbvh_share_queries_workspace_size(m, dim), device)
+    count = ctypes.c_int64(0)
+    _check(lib.tbvh_share_queries(device.index, queries.data_ptr(), m, dim, scene_min.contiguous().data_ptr(),
+                                  scene_max.contiguous().data_ptr(), int(rank), int(world), int(chunk),
+                                  out.data_ptr(), ctypes.byref(count), ws.data_ptr(), ws.numel(), _stream(device)))
+    return out[: count.value]
 
 
 def morton_sort_queries_ragged(queries: torch.Tensor, query_offsets: torch.Tensor, total: int,

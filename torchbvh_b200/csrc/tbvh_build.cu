@@ -826,6 +826,145 @@ __global__ void __launch_bounds__(256) k_selftest_prepare(uint32_t* keys, int64_
   if (blockIdx.x == 0 && threadIdx.x == 0) *tile_ctr = 1u;
 }
 
+// ---------------------------------------------------------------------------
+// One rank's share of the queries of one cloud (sharded single-cloud k-NN).
+//
+// The Morton-code range is cut at the granularity of its top kShareBits bits
+// ("cells"): a histogram of the cells, then an ownership table that walks the
+// cells in code order and hands consecutive runs of about `chunk` queries to
+// the ranks in turn (one run per rank when chunk = M / world: contiguous
+// Morton ranges; smaller chunks interleave the ranks over the whole cloud so
+// that each rank sees every kind of region). Each rank then compacts only its
+// own queries and sorts them by Morton code, instead of sorting all M. Every
+// rank computes the same histogram and table, so no exchange is needed.
+// ---------------------------------------------------------------------------
+constexpr int kShareBits = 15;
+constexpr int kShareCells = 1 << kShareBits;
+constexpr int kShareThreads = 1024;
+
+template <int D>
+__global__ void __launch_bounds__(kShareThreads) k_share_cells(const float* __restrict__ q, int64_t m,
+                                                               const float* __restrict__ smin,
+                                                               const float* __restrict__ smax,
+                                                               uint32_t* __restrict__ codes,
+                                                               uint32_t* __restrict__ cell_count) {
+  extern __shared__ uint32_t s_cells[];  // kShareCells counters
+  for (int i = threadIdx.x; i < kShareCells; i += blockDim.x) s_cells[i] = 0u;
+  float lo[D], hi[D];
+#pragma unroll
+  for (int a = 0; a < D; ++a) { lo[a] = smin[a]; hi[a] = smax[a]; }
+  __syncthreads();
+  constexpr int shift = morton_bits<D>() - kShareBits;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < m; i += int64_t(gridDim.x) * blockDim.x) {
+    float p[D];
+#pragma unroll
+    for (int a = 0; a < D; ++a) p[a] = q[i * D + a];
+    const uint32_t code = morton_code<D>(p, lo, hi);
+    codes[i] = code;
+    atomicAdd(&s_cells[code >> shift], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kShareCells; i += blockDim.x) {
+    const uint32_t v = s_cells[i];
+    if (v) atomicAdd(cell_count + i, v);
+  }
+}
+
+// One block: exclusive scan of the cell counts in code order, owner of each
+// cell = (queries before it / chunk) mod world, per-rank totals.
+__global__ void __launch_bounds__(kShareThreads) k_share_owners(const uint32_t* __restrict__ cell_count,
+                                                                int64_t chunk, int world,
+                                                                uint8_t* __restrict__ owner,
+                                                                int64_t* __restrict__ rank_count) {
+  constexpr int per = kShareCells / kShareThreads;
+  __shared__ int64_t s_warp[kShareThreads / 32];
+  int64_t local[per];
+  int64_t sum = 0;
+#pragma unroll
+  for (int j = 0; j < per; ++j) {
+    local[j] = cell_count[threadIdx.x * per + j];
+    sum += local[j];
+  }
+  // Block-wide exclusive scan of the per-thread sums.
+  const unsigned lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  int64_t x = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t y = __shfl_up_sync(kFullMask, x, o);
+    if (lane >= unsigned(o)) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = s_warp[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(kFullMask, w, o);
+      if (lane >= unsigned(o)) w += y;
+    }
+    s_warp[lane] = w;
+  }
+  __syncthreads();
+  int64_t before = (warp == 0 ? 0 : s_warp[warp - 1]) + x - sum;
+#pragma unroll
+  for (int j = 0; j < per; ++j) {
+    const int r = int((before / chunk) % world);
+    owner[threadIdx.x * per + j] = uint8_t(r);
+    if (local[j]) atomicAdd(reinterpret_cast<unsigned long long*>(rank_count + r),
+                            static_cast<unsigned long long>(local[j]));
+    before += local[j];
+  }
+}
+
+// Appends this rank's queries (code, index) and accumulates the digit
+// histograms of every sort pass over them. Warp-aggregated appends: the order
+// among appended queries is arbitrary, which only decides the order of equal
+// codes after the sort (each query's result does not depend on it).
+template <int D>
+__global__ void __launch_bounds__(256) k_share_compact(const uint32_t* __restrict__ codes, int64_t m,
+                                                       const uint8_t* __restrict__ owner, int rank,
+                                                       uint32_t* __restrict__ out_keys,
+                                                       uint32_t* __restrict__ out_vals,
+                                                       unsigned long long* __restrict__ counter,
+                                                       uint32_t* __restrict__ hist, int passes,
+                                                       int64_t capacity, unsigned* status) {
+  __shared__ uint32_t s_hist[kMaxSortPasses][kRadix];
+  for (int i = threadIdx.x; i < kMaxSortPasses * kRadix; i += blockDim.x) (&s_hist[0][0])[i] = 0u;
+  __syncthreads();
+  constexpr int shift = morton_bits<D>() - kShareBits;
+  const unsigned lane = threadIdx.x & 31u;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t rounds = (m + stride - 1) / stride;
+  for (int64_t r = 0; r < rounds; ++r) {
+    const int64_t i = r * stride + int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t code = 0;
+    bool mine = false;
+    if (i < m) {
+      code = codes[i];
+      mine = owner[code >> shift] == rank;
+    }
+    const unsigned take = __ballot_sync(kFullMask, mine);
+    unsigned long long base = 0;
+    if (lane == 0 && take) base = atomicAdd(counter, static_cast<unsigned long long>(__popc(take)));
+    base = __shfl_sync(kFullMask, base, 0);
+    if (mine) {
+      const int64_t pos = int64_t(base) + __popc(take & ((1u << lane) - 1u));
+      if (pos < capacity) {
+        out_keys[pos] = code;
+        out_vals[pos] = uint32_t(i);
+        for (int ps = 0; ps < passes; ++ps) atomicAdd(&s_hist[ps][(code >> (8 * ps)) & 0xffu], 1u);
+      } else {
+        device_error(status, kDevErrBadIndex);
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < passes * kRadix; i += blockDim.x) {
+    const uint32_t v = (&s_hist[0][0])[i];
+    if (v) atomicAdd(hist + i, v);
+  }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -953,9 +1092,10 @@ static int grid_for(int64_t work, int per_block, int cap) {
   return int(g);
 }
 
-// Runs the radix passes over keys already in ss.keys[0] (values implicit).
+// Runs the radix passes over keys already in ss.keys[0]; the values of the
+// first pass are ss.vals[0] when explicit_vals, else the element index.
 static cudaError_t run_sort_passes(const SortPlan& p, const SortScratch& ss, const CloudMap& cm,
-                                   int64_t* final_out, cudaStream_t stream) {
+                                   int64_t* final_out, cudaStream_t stream, bool explicit_vals = false) {
   const size_t smem = sizeof(PassSmem);
   static_assert(sizeof(PassSmem) <= 48 * 1024, "pass tile must fit the default dynamic shared memory limit");
   unsigned* status = device_status_ptr();
@@ -963,7 +1103,7 @@ static cudaError_t run_sort_passes(const SortPlan& p, const SortScratch& ss, con
   for (int ps = 0; ps < p.passes; ++ps) {
     PassArgs a{};
     a.keys_in = ss.keys[src];
-    a.vals_in = ps == 0 ? nullptr : ss.vals[src];
+    a.vals_in = ps == 0 ? (explicit_vals ? ss.vals[0] : nullptr) : ss.vals[src];
     const bool last = ps == p.passes - 1;
     a.keys_out = last ? nullptr : ss.keys[src ^ 1];
     a.vals_out = last ? nullptr : ss.vals[src ^ 1];
@@ -1072,6 +1212,96 @@ cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   return run_sort_passes(p, q.ss, q.clouds, q.order_out, stream);
+}
+
+// ---- one rank's query share -------------------------------------------------
+namespace {
+constexpr int kShareMaxWorld = 256;
+
+struct ShareScratch {
+  uint32_t* codes;
+  uint32_t* cell_count;
+  uint8_t* owner;
+  int64_t* rank_count;
+  unsigned long long* counter;
+  SortScratch ss;
+};
+
+void carve_share(int64_t m, int dim, char*& cur, ShareScratch& s) {
+  auto take = [&](size_t bytes) { char* r = cur; cur += align_up(bytes, 256); return r; };
+  s.codes = reinterpret_cast<uint32_t*>(take(size_t(m) * 4));
+  s.cell_count = reinterpret_cast<uint32_t*>(take(size_t(kShareCells) * 4));
+  s.owner = reinterpret_cast<uint8_t*>(take(size_t(kShareCells)));
+  s.rank_count = reinterpret_cast<int64_t*>(take(size_t(kShareMaxWorld) * 8));
+  s.counter = reinterpret_cast<unsigned long long*>(take(8));
+  carve_sort_scratch(make_sort_plan(m, 1, dim), cur, s.ss);
+}
+}  // namespace
+
+size_t share_scratch_bytes(int64_t m, int dim) {
+  return align_up(size_t(m) * 4, 256) + align_up(size_t(kShareCells) * 4, 256) + align_up(size_t(kShareCells), 256) +
+         align_up(size_t(kShareMaxWorld) * 8, 256) + align_up(8, 256) + sort_scratch_bytes(make_sort_plan(m, 1, dim));
+}
+
+cudaError_t launch_share_queries(const ShareLaunch& q, int64_t* count_out, cudaStream_t stream) {
+  const int64_t m = q.num_queries;
+  const int D = q.dim;
+  char* cur = static_cast<char*>(q.workspace);
+  ShareScratch s;
+  carve_share(m, D, cur, s);
+  const SortPlan full = make_sort_plan(m, 1, D);
+  InitArgs ia{};
+  ia.zero[0] = {s.cell_count, int64_t(kShareCells)};
+  ia.zero[1] = {reinterpret_cast<uint32_t*>(s.rank_count), int64_t(kShareMaxWorld) * 2 + 2};  // + counter
+  ia.zero[2] = {reinterpret_cast<uint32_t*>(s.ss.lookback[0]), full.tiles * kRadix * 2};
+  ia.zero[3] = {s.ss.hist, int64_t(kMaxSortPasses) * kRadix + kMaxSortPasses};           // + tile counters
+  k_init<<<grid_for(full.tiles * kRadix * 2, 256 * 4, 1184), 256, 0, stream>>>(ia);
+  count_launches(1);
+  const size_t cells_smem = size_t(kShareCells) * 4;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = D == 3 ? cudaFuncSetAttribute(k_share_cells<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  int(cells_smem))
+                           : cudaFuncSetAttribute(k_share_cells<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  int(cells_smem));
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  // Blocks of 1,024 threads with a 128 KB cell histogram each: about 128 K
+  // queries per block keeps the per-block flush of the table cheap.
+  const int cgrid = grid_for(m, kShareThreads * 128, 148 * 2);
+  if (D == 3)
+    k_share_cells<3><<<cgrid, kShareThreads, cells_smem, stream>>>(q.queries, m, q.scene_min, q.scene_max, s.codes,
+                                                                    s.cell_count);
+  else
+    k_share_cells<2><<<cgrid, kShareThreads, cells_smem, stream>>>(q.queries, m, q.scene_min, q.scene_max, s.codes,
+                                                                    s.cell_count);
+  k_share_owners<<<1, kShareThreads, 0, stream>>>(s.cell_count, q.chunk, q.world, s.owner, s.rank_count);
+  const int pgrid = grid_for(m, 256, 148 * 8);
+  if (D == 3)
+    k_share_compact<3><<<pgrid, 256, 0, stream>>>(s.codes, m, s.owner, q.rank, s.ss.keys[0], s.ss.vals[0],
+                                                   s.counter, s.ss.hist, full.passes, m, device_status_ptr());
+  else
+    k_share_compact<2><<<pgrid, 256, 0, stream>>>(s.codes, m, s.owner, q.rank, s.ss.keys[0], s.ss.vals[0],
+                                                   s.counter, s.ss.hist, full.passes, m, device_status_ptr());
+  count_launches(3);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  int64_t count = 0;
+  e = cudaMemcpyAsync(&count, s.rank_count + q.rank, sizeof(int64_t), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return e;
+  if (count < 0 || count > m) count = 0;
+  *count_out = count;
+  if (count == 0) return cudaSuccess;
+  SortPlan plan = make_sort_plan(count, 1, D);
+  CloudMap cm{};
+  cm.offsets = nullptr;
+  cm.uniform_n = m;
+  cm.num_clouds = 1;
+  return run_sort_passes(plan, s.ss, cm, q.share_out, stream, /*explicit_vals=*/true);
 }
 
 }  // namespace tbvh

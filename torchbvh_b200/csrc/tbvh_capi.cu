@@ -301,6 +301,46 @@ int tbvh_sort_queries(int device, const float* queries, int64_t num_clouds, int6
   return TBVH_OK;
 }
 
+size_t tbvh_share_queries_workspace_size(int64_t num_queries, int dim) {
+  if (num_queries < 1 || num_queries > INT_MAX || (dim != 2 && dim != 3)) return 0;
+  return tbvh::share_scratch_bytes(num_queries, dim);
+}
+
+int tbvh_share_queries(int device, const float* queries, int64_t num_queries, int dim, const float* scene_min,
+                       const float* scene_max, int rank, int world, int64_t chunk, int64_t* share_out,
+                       int64_t* share_count, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "share_queries";
+  g_last_error.clear();
+  if (dim != 2 && dim != 3) return fail(TBVH_ERR_BAD_ARG, "%s: D must be 2 or 3", op);
+  if (num_queries < 1 || num_queries > INT_MAX)
+    return fail(TBVH_ERR_BAD_ARG, "%s: query count must be in [1, 2^31)", op);
+  if (world < 1 || world > 256 || rank < 0 || rank >= world)
+    return fail(TBVH_ERR_BAD_ARG, "%s: need 0 <= rank < world <= 256", op);
+  if (chunk < 1) return fail(TBVH_ERR_BAD_ARG, "%s: chunk must be >= 1", op);
+  if (!queries || !scene_min || !scene_max || !share_out || !share_count)
+    return fail(TBVH_ERR_BAD_ARG, "%s: NULL pointer", op);
+  const size_t need = tbvh::share_scratch_bytes(num_queries, dim);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(TBVH_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the required %zu", op,
+                workspace_bytes, need);
+  int rc = set_device(device, op);
+  if (rc) return rc;
+  tbvh::ShareLaunch q{};
+  q.queries = queries;
+  q.num_queries = num_queries;
+  q.dim = dim;
+  q.scene_min = scene_min;
+  q.scene_max = scene_max;
+  q.rank = rank;
+  q.world = world;
+  q.chunk = chunk;
+  q.share_out = share_out;
+  q.workspace = workspace;
+  cudaError_t e = tbvh::launch_share_queries(q, share_count, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, op);
+  return TBVH_OK;
+}
+
 size_t tbvh_query_knn_workspace_size(int64_t num_clouds, int64_t points_per_cloud) {
   if (num_clouds < 1) return 0;
   if (points_per_cloud > 0) return 256;

@@ -117,7 +117,7 @@ __host__ __device__ inline uint32_t morton_code(const float* p, const float* lo,
 }
 
 template <int D>
-constexpr int morton_bits() { return D == 3 ? 30 : 32; }
+__host__ __device__ constexpr int morton_bits() { return D == 3 ? 30 : 32; }
 
 // ---------------------------------------------------------------------------
 // Squared distances. Same float32 operation sequence as the reference's

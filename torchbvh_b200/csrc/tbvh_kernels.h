@@ -105,6 +105,24 @@ struct QuerySortLaunch {
 
 cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream);
 
+// One rank's share of the queries of one cloud, in Morton order (see
+// k_share_cells in tbvh_build.cu). Synchronous: the share size comes back to
+// the host (*count_out) before the share is sorted.
+struct ShareLaunch {
+  const float* queries;
+  int64_t num_queries;
+  int dim;
+  const float* scene_min;
+  const float* scene_max;
+  int rank;
+  int world;
+  int64_t chunk;        // queries per ownership run (M / world: contiguous Morton ranges)
+  int64_t* share_out;   // capacity num_queries
+  void* workspace;      // share_scratch_bytes(num_queries, dim)
+};
+size_t share_scratch_bytes(int64_t m, int dim);
+cudaError_t launch_share_queries(const ShareLaunch& q, int64_t* count_out, cudaStream_t stream);
+
 // ---- k-NN traversal ----------------------------------------------------------
 constexpr int kMaxDest = 8;  // result destinations of one k-NN launch (GPUs of one node)
 struct KnnLaunch {

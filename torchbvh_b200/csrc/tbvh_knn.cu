@@ -47,16 +47,28 @@ constexpr int kKnnWarps = kKnnThreads / 32;
 constexpr int kBucketLevels = TBVH_KNN_BUCKET_LEVELS;  // bucket = 2^levels leaves (<= 32)
 constexpr int kBucketSize = 1 << kBucketLevels;
 static_assert(kBucketSize <= 32, "a bucket is staged by one warp");
-constexpr int kStackDepth = 28;   // >= deepest bucket level + 1 for N < 2^31 (27)
+// Deferred nodes: at most 3 per two-level step (one per level for a binary
+// step) down to the bucket level, which is <= 26 for N < 2^31.
+constexpr int kStackDepth = 44;
 // Smallest k kept as a shared-memory heap (smaller k: register list).
 #ifndef TBVH_KNN_HEAP_MIN_K
 #define TBVH_KNN_HEAP_MIN_K 16
 #endif
 // 1: the stack keeps each lane's bound of a deferred node; 0: the bound is
-// recomputed from the node box when the node is popped (less shared memory).
+// recomputed from the node box when the node is popped. Recomputing costs a
+// warp-uniform box load per pop but frees 5.5 KB of shared memory per warp,
+// which on B200 buys more resident warps (c4: 53 ms against 69 ms).
 #ifndef TBVH_KNN_STACK_BOUNDS
-#define TBVH_KNN_STACK_BOUNDS 1
+#define TBVH_KNN_STACK_BOUNDS 0
 #endif
+// 1: above the last level before the buckets, a step tests the four
+// grandchildren of the node (four consecutive rows of node_aabbs) and skips
+// the children's level: half the steps and stack traffic, four independent
+// box loads per step. 0: binary steps.
+#ifndef TBVH_KNN_WIDE
+#define TBVH_KNN_WIDE 1
+#endif
+constexpr bool kWideSteps = TBVH_KNN_WIDE != 0;
 constexpr bool kStackBounds = TBVH_KNN_STACK_BOUNDS != 0;
 // Seeding window: this many times k sorted leaves around the query's rank.
 #ifndef TBVH_KNN_SEED_WINDOW
@@ -467,6 +479,79 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
         }
         __syncwarp();
         KNN_PF_LAP(4);
+      } else if (kWideSteps && level + 2 <= Lb) {
+        // Two levels at once: the node's four grandchildren are four consecutive
+        // rows of the next-but-one level (the first is always real). A
+        // grandchild box lies inside its parent's, so skipping the parents'
+        // level never admits a node the binary walk would have pruned.
+        const int gl = level + 2;
+        const int64_t g0 = node * 4;
+        const int64_t gleft = __shfl_sync(kFullMask, my_cnt, gl) - g0;
+        const int64_t grow = __shfl_sync(kFullMask, my_rowoff, gl) + g0;
+        float dg[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          dg[g] = INFINITY;
+          if (g < gleft) {
+            float lo[D], hi[D];
+            load_box<D>(rows, grow + g, lo, hi);
+            dg[g] = box_dist2<D>(q, lo, hi);
+          }
+        }
+        // Warp-uniform order: the admitted grandchildren by how many lanes find
+        // each one their nearest admitted box (ties: lower index first).
+        int best = -1;
+        float best_d = INFINITY;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (dg[g] <= kth && dg[g] < best_d) {
+            best_d = dg[g];
+            best = g;
+          }
+        }
+        int key[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const bool admitted = __any_sync(kFullMask, dg[g] <= kth);
+          const int votes = __popc(__ballot_sync(kFullMask, best == g));
+          key[g] = admitted ? (votes << 2) | (3 - g) : -1;
+        }
+        auto swap_desc = [](int& x, int& y) {
+          const int hi = x > y ? x : y;
+          y = x > y ? y : x;
+          x = hi;
+        };
+        swap_desc(key[0], key[1]);
+        swap_desc(key[2], key[3]);
+        swap_desc(key[0], key[2]);
+        swap_desc(key[1], key[3]);
+        swap_desc(key[1], key[2]);
+        // Defer the others, least preferred deepest.
+#pragma unroll
+        for (int r = 3; r >= 1; --r) {
+          if (key[r] >= 0) {
+            const int g = 3 - (key[r] & 3);
+            if (sp < kStackDepth) {
+              if constexpr (kStackBounds) {
+                s.stack_dist[warp][sp][lane] = g == 0 ? dg[0] : g == 1 ? dg[1] : g == 2 ? dg[2] : dg[3];
+              }
+              if (lane == 0) s.stack_node[warp][sp] = uint32_t(g0 + g) | (uint32_t(gl) << 27);
+              ++sp;
+            } else if (lane == 0) {
+              atomicOr(a.status, kDevErrStackOverflow);
+            }
+          }
+        }
+        KNN_PF_CNT(8, 1);
+        if (key[0] >= 0) {
+          const int g = 3 - (key[0] & 3);
+          level = gl;
+          node = g0 + g;
+          nd = g == 0 ? dg[0] : g == 1 ? dg[1] : g == 2 ? dg[2] : dg[3];
+          KNN_PF_LAP(2);
+          continue;
+        }
+        KNN_PF_LAP(2);
       } else {
         const int cl = level + 1;
         const int64_t c0 = node * 2;
@@ -586,7 +671,10 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
       // cloud's last point, as PyTorch's negative indexing would.
       const float* src = a.src_points + pt_off * D;
       float* op = a.out_pos + row * K * D;
-#pragma unroll 4
+      // Register lists need constant slot indices (full unroll); heap slots are
+      // shared-memory reads, so four at a time keep few loads in flight.
+      constexpr int kGatherUnroll = kHeap ? 4 : K;
+#pragma unroll kGatherUnroll
       for (int i = 0; i < K; ++i) {
         int64_t idx = key_idx(top.at(i));
         if (idx < 0) idx = n - 1;

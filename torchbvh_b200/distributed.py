@@ -80,19 +80,38 @@ def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Ten
     return torch.cat([b[:c] for b, c in zip(bufs, counts)])
 
 
-def _morton_share_cuda(points: torch.Tensor, queries: torch.Tensor, k: int, q0: int, q1: int):
-    """One BVH build; the queries' Morton order against its scene box; k-NN of
-    sorted positions [q0, q1) with the slice already in traversal order."""
-    from ._bvh_class import BVH
-    from ._native import _C
+SPLITS = ("morton", "interleaved", "contiguous")
+_RUNS_PER_RANK = 32  # ownership runs per rank of the interleaved split
 
-    with BVH(points) as bvh:
-        h = bvh._handle
-        order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
-                                              h["scene_max"].unsqueeze(0))[0]
-        mine = order[q0:q1]
-        idx, dist_sq = bvh.knn(queries.index_select(0, mine), k, sort_queries=False)
-    return order, mine, idx, dist_sq
+
+def _split_chunk(m: int, world: int, split: str) -> int:
+    """Queries per ownership run: one run per rank ("morton"), or 32 runs per rank
+    dealt round-robin over the Morton order ("interleaved")."""
+    if split == "morton":
+        return -(-m // world)
+    return max(1, -(-m // (world * _RUNS_PER_RANK)))
+
+
+def _owned_by_order(order: torch.Tensor, m: int, world: int, rank: int, split: str) -> torch.Tensor:
+    """This rank's queries from a full traversal order (CPU paths and tests): the
+    positions of `order` whose run (position // chunk) the rank owns."""
+    chunk = _split_chunk(m, world, split)
+    runs = torch.arange(m, device=order.device) // chunk
+    return order[runs % world == rank]
+
+
+def _owned_queries_cuda(handle, queries: torch.Tensor, rank: int, world: int, split: str) -> torch.Tensor:
+    """This rank's query indices in traversal order on the CUDA path. Morton
+    splits select and sort only the rank's own share (tbvh_share_queries);
+    every rank derives the same split, so the shares partition the queries."""
+    from ._native import share_queries
+
+    m = queries.shape[0]
+    if split == "contiguous":
+        q0, q1 = shard_range(m, world, rank)
+        return torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
+    return share_queries(queries, handle["scene_min"], handle["scene_max"], rank, world,
+                         _split_chunk(m, world, split))
 
 
 class PeerResults:
@@ -168,21 +187,16 @@ class PeerResults:
         self.close()
 
 
-def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, q0: int, q1: int, split: str,
+def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, rank: int, world: int, split: str,
                     out: PeerResults):
-    """One BVH build; this rank's share of the queries (a range of their Morton
-    order, or of their given order); results delivered to every rank's `out`."""
+    """One BVH build; this rank's share of the queries; results delivered to
+    every rank's `out`."""
     from ._bvh_class import BVH
-    from ._native import _C, query_knn_share
+    from ._native import query_knn_share
 
     with BVH(points) as bvh:
         h = bvh._handle
-        if split == "morton":
-            order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
-                                                  h["scene_max"].unsqueeze(0))[0]
-            share = order[q0:q1]
-        else:
-            share = torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
+        share = _owned_queries_cuda(h, queries, rank, world, split)
         # No rank may store into a peer's buffers while that peer still reads the
         # previous call's rows: a collective on every rank's current stream, after
         # its earlier reads and before any traversal, orders them.
@@ -201,21 +215,32 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     """Exact k-NN of one cloud with the queries split over ranks.
 
     `points` is read on rank `src` only (other ranks may pass None); every rank
-    passes the full `queries` tensor. `split`: "morton" gives each rank a
-    contiguous range of the queries' Morton order (computed on every rank
-    against the shared BVH, or by `order_fn(points, queries)` when given),
-    "contiguous" a contiguous range of the given order. `gather`: "all"
-    returns the full (M, k) results in the original query order on every rank,
-    "root" only on `src` (None elsewhere), "none" returns this rank's rows and
-    which queries they belong to (the (start, end) range for "contiguous", the
-    int64 query indices for "morton").
+    passes the full `queries` tensor. `split` ("morton", "interleaved",
+    "contiguous") decides which queries each rank serves:
+
+    * "morton": one contiguous range of the queries' Morton order (codes
+      against the shared BVH's scene box), of nearly equal size per rank;
+    * "interleaved": runs of the Morton order (32 per rank) dealt to the ranks
+      in turn, so that every rank gets queries from every region of the cloud
+      and the per-rank cost evens out;
+    * "contiguous": a contiguous slice of the given query order.
+
+    On the CUDA path each rank selects and sorts only its own share. With
+    `order_fn(points, queries)` (a full traversal order) or a custom
+    `knn_fn`, the Morton splits are taken from `order_fn`'s order (default:
+    this package's Morton sort).
+
+    `gather`: "all" returns the full (M, k) results in the original query order
+    on every rank, "root" only on `src` (None elsewhere), "none" returns this
+    rank's rows and which queries they belong to (the (start, end) range for
+    "contiguous", else the int64 query indices).
 
     `out` (a PeerResults, gather="all" with the CUDA path only): the traversal
     itself delivers every row to every rank; the returned tensors are views of
     `out`, valid until the next call with it.
     """
-    if split not in ("morton", "contiguous"):
-        raise ValueError("knn_sharded_single_cloud: split must be 'morton' or 'contiguous'")
+    if split not in SPLITS:
+        raise ValueError("knn_sharded_single_cloud: split must be 'morton', 'interleaved' or 'contiguous'")
     world, rank = _world(group)
     dev = device or queries.device
     buf = points if rank == src else torch.empty((num_points, dim), dtype=torch.float32, device=dev)
@@ -223,42 +248,66 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     dist.broadcast(buf, src=src, group=group)
     m = queries.shape[0]
     q0, q1 = shard_range(m, world, rank)
+    queries = queries.contiguous()
     if out is not None:
         if gather != "all" or knn_fn is not default_knn or order_fn is not None:
             raise ValueError("knn_sharded_single_cloud: out= needs gather='all' and the CUDA path")
         if out.num_queries != m or out.k != k:
             raise ValueError("knn_sharded_single_cloud: out= was made for another query count or k")
-        return _share_to_peers(buf, queries.contiguous(), k, q0, q1, split, out)
-    order = None
+        return _share_to_peers(buf, queries, k, rank, world, split, out)
     if split == "contiguous":
         idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
-        owned = (q0, q1)
+        owned = torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
     elif order_fn is None and knn_fn is default_knn:
-        order, owned, idx, dist_sq = _morton_share_cuda(buf, queries, k, q0, q1)
+        from ._bvh_class import BVH
+
+        with BVH(buf) as bvh:
+            owned = _owned_queries_cuda(bvh._handle, queries, rank, world, split)
+            idx, dist_sq = bvh.knn(queries.index_select(0, owned), k, sort_queries=False)
     else:
-        order = order_fn(buf, queries) if order_fn is not None else _morton_share_cuda(buf, queries, k, 0, 0)[0]
-        owned = order[q0:q1]
+        order = order_fn(buf, queries) if order_fn is not None else _full_morton_order(buf, queries)
+        owned = _owned_by_order(order, m, world, rank, split)
         idx, dist_sq = knn_fn(buf, queries.index_select(0, owned).contiguous(), k)
     if gather == "none":
-        return idx, dist_sq, owned
-    counts = [shard_range(m, world, r)[1] - shard_range(m, world, r)[0] for r in range(world)]
+        return idx, dist_sq, ((q0, q1) if split == "contiguous" else owned)
+    counts = _share_sizes(owned.numel(), group, owned.device)
     if gather == "root":
         idx_all = _gather_to(idx, counts, src, group)
         dist_all = _gather_to(dist_sq, counts, src, group)
+        owners = _gather_to(owned.unsqueeze(1), counts, src, group)
         if rank != src:
             return None, None
-        return _to_query_order(idx_all, order), _to_query_order(dist_all, order)
+        return _to_query_order(idx_all, owners[:, 0]), _to_query_order(dist_all, owners[:, 0])
     idx_all = _all_gather_rows(idx, counts, group)
     dist_all = _all_gather_rows(dist_sq, counts, group)
-    return _to_query_order(idx_all, order), _to_query_order(dist_all, order)
+    owners = _all_gather_rows(owned.unsqueeze(1), counts, group)[:, 0]
+    return _to_query_order(idx_all, owners), _to_query_order(dist_all, owners)
 
 
-def _to_query_order(rows: torch.Tensor, order: torch.Tensor | None) -> torch.Tensor:
-    """Rows in split order -> rows in query order (row p of `rows` belongs to query order[p])."""
-    if order is None:
-        return rows
+def _full_morton_order(points: torch.Tensor, queries: torch.Tensor) -> torch.Tensor:
+    """All queries in Morton order against the points' BVH (CUDA)."""
+    from ._bvh_class import BVH
+    from ._native import _C
+
+    with BVH(points) as bvh:
+        h = bvh._handle
+        return _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                             h["scene_max"].unsqueeze(0))[0]
+
+
+def _share_sizes(n: int, group, device: torch.device) -> list[int]:
+    """Every rank's share size (one small all-gather)."""
+    world, _ = _world(group)
+    mine = torch.tensor([n], dtype=torch.int64, device=device)
+    sizes = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(sizes, mine, group=group)
+    return [int(s.item()) for s in sizes]
+
+
+def _to_query_order(rows: torch.Tensor, owners: torch.Tensor) -> torch.Tensor:
+    """Rows gathered rank by rank -> rows in query order (row p belongs to query owners[p])."""
     out = torch.empty_like(rows)
-    out.index_copy_(0, order.to(rows.device), rows)
+    out.index_copy_(0, owners.to(rows.device), rows)
     return out
 
 
