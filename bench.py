@@ -67,9 +67,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--c4-points", type=int, default=16_777_216,
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
-    ap.add_argument("--c4-split", default="morton", choices=["morton", "contiguous"],
-                    help="c4 on N > 1 GPUs: share of the queries per rank (a range of their Morton order, "
-                         "or of their given order)")
+    ap.add_argument("--c4-split", default="morton", choices=["morton", "interleaved", "contiguous"],
+                    help="c4 on N > 1 GPUs: share of the queries per rank (one range of their Morton order, "
+                         "runs of it dealt to the ranks in turn, or a range of their given order)")
     return ap.parse_args()
 
 
@@ -517,9 +517,11 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
     if not args.no_e2e:
         hp = w.points.pin_memory() if rank == 0 else None
         hq = w.queries.pin_memory()
-        q0, q1 = tdist.shard_range(m, world, rank)
-        host_idx = torch.empty((q1 - q0, k), dtype=torch.int64).pin_memory()
-        host_dist = torch.empty((q1 - q0, k), dtype=torch.float32).pin_memory()
+        # The rank's share size depends on the split; it is the same every step.
+        share_rows = int(step(points, queries, "none")[2].numel()) if args.c4_split != "contiguous" else \
+            tdist.shard_range(m, world, rank)[1] - tdist.shard_range(m, world, rank)[0]
+        host_idx = torch.empty((share_rows, k), dtype=torch.int64).pin_memory()
+        host_dist = torch.empty((share_rows, k), dtype=torch.float32).pin_memory()
 
         def e2e_inputs():
             p = hp.to(device, non_blocking=True) if rank == 0 else None
@@ -545,7 +547,7 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         e2e_ms = max_over_ranks(e2e_step_ms(e2e_steps), world)
         e2e = {"value": m * e2e_steps / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": (n * dim * 4 if rank == 0 else 0) + m * dim * 4,
-               "d2h_bytes_per_step": (q1 - q0) * k * 12,
+               "d2h_bytes_per_step": share_rows * k * 12,
                "ms_per_step": e2e_ms / e2e_steps,
                "api": "torchbvh_b200.distributed.knn_sharded_single_cloud(..., gather='none') from pinned host "
                       "buffers (byte counts of rank 0)"}

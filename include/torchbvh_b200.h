@@ -178,7 +178,9 @@ int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* so
  *
  * Buffers that other GPUs write into are shared with CUDA IPC:
  * tbvh_peer_alloc allocates `bytes` (rounded up to whole 2 MiB, so that the
- * buffer is an allocation of its own) on `device` (cudaMalloc) and fills
+ * buffer is an allocation of its own, which it then verifies with the
+ * driver's cuMemGetAddressRange and refuses to share otherwise) on `device`
+ * (cudaMalloc) and fills
  * out_handle (tbvh_peer_handle_bytes() bytes) for the other processes;
  * tbvh_peer_open maps such a handle on `device` (point-to-point mapping, no
  * multicast); tbvh_peer_close / tbvh_peer_free undo them. Synchronous.

@@ -36,8 +36,11 @@ namespace tbvh {
 namespace {
 
 // Tuning knobs (compile-time; the defaults are the measured best on B200).
+// One warp per block: a block's resources are released as soon as its warp
+// ends, so a slow warp never holds idle warps' slots (c4: 46.9 ms against
+// 52.7 ms with four-warp blocks).
 #ifndef TBVH_KNN_THREADS
-#define TBVH_KNN_THREADS 128
+#define TBVH_KNN_THREADS 32
 #endif
 constexpr int kKnnThreads = TBVH_KNN_THREADS;
 constexpr int kKnnWarps = kKnnThreads / 32;
@@ -76,12 +79,27 @@ constexpr bool kStackBounds = TBVH_KNN_STACK_BOUNDS != 0;
 #endif
 constexpr int kSeedWindow = TBVH_KNN_SEED_WINDOW;
 static_assert(kSeedWindow >= 1, "the window must hold at least k leaves");
+// 1: the warp seeds every lane from the union of the lanes' windows (at most
+// kUnionCap leaves, staged through shared memory); 0: each lane its own window.
+// Measured on B200 (traversal ms, union / own window): c4 47.6 / 46.8, c2 1.96 /
+// 1.88, c3 1.31 / 1.07, c5 42.4 / 43.8: the richer seed does not repay its
+// extra insertions except on the ragged anisotropic clouds.
+#ifndef TBVH_KNN_UNION_SEED
+#define TBVH_KNN_UNION_SEED 0
+#endif
+constexpr bool kUnionSeed = TBVH_KNN_UNION_SEED != 0;
+#ifndef TBVH_KNN_UNION_CAP
+#define TBVH_KNN_UNION_CAP 256
+#endif
+constexpr int64_t kUnionCap = TBVH_KNN_UNION_CAP;
+static_assert(TBVH_KNN_UNION_CAP >= 32, "the union holds at least k <= 32 leaves");
 // Developer option: -DTBVH_KNN_PROFILE=1 sums, over warps, the clock cycles
 // of each traversal phase and counts of its events into g_knn_profile
 // (slots: 0 rank search, 1 seeding window, 2 node steps, 3 bucket load + marks,
-// 4 insertion rounds, 5 stack pops, 6 heap sort + row writes; 8 node steps,
-// 9 buckets, 10 insertion rounds, 11 insertions, 12 pops, 13 warp passes,
-// 14 active lanes). Off by default; timings taken with it on are not reported.
+// 4 insertion rounds, 5 stack pops, 6 heap sort + row writes; 7 bucket marks
+// and 11 insertions of one lane per warp; 8 node steps, 9 buckets, 10
+// insertion rounds, 12 pops, 13 warp passes, 14 active lanes). Off by default;
+// timings taken with it on are not reported.
 #ifndef TBVH_KNN_PROFILE
 #define TBVH_KNN_PROFILE 0
 #endif
@@ -368,14 +386,73 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
     }
   };
 
+  // Stages sorted leaves [start, start + count) (count <= 32) into the warp's
+  // shared buffer with one coalesced load: coordinates and original index.
+  auto stage_leaves = [&](int64_t start, int count) {
+    if (int(lane) < count) {
+      float p[D];
+      load_leaf<D>(rows, leaf_row0 + start + lane, p);
+      const int32_t src = int32_t(sorted[start + lane]);
+      s.bucket[warp][lane] = make_float4(p[0], p[1], D == 3 ? p[2] : 0.0f, __int_as_float(src));
+    }
+    __syncwarp();
+  };
+  // Offers the staged points [from, count) to every lane: pass 1 marks those
+  // within the lane's current k-th distance (less the `skip` bits), pass 2
+  // inserts the marked points, one per lane per round.
+  auto mark_and_insert = [&](int from, int count, uint32_t skip) {
+    uint32_t cand = 0;
+    if (from == 0 && count == 32) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float4 p = s.bucket[warp][i];
+        if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
+      }
+    } else {
+      for (int i = from; i < count; ++i) {
+        const float4 p = s.bucket[warp][i];
+        if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
+      }
+    }
+    cand &= ~skip;
+    __syncwarp();
+    KNN_PF_LAP(3);
+    KNN_PF_CNT(7, __popc(cand));
+    while (__any_sync(kFullMask, cand != 0u)) {
+      KNN_PF_CNT(10, 1);
+      if (cand) {
+        // Marks were taken against the k-th distance at the start of the
+        // pass; insertions since may have lowered it. A lane first skips, in
+        // a cheap per-lane loop, marks that no longer beat its k-th key, so a
+        // round (one insertion) is only spent on one that does.
+        u64 nk;
+        bool take;
+        do {
+          const int i = __ffs(cand) - 1;
+          cand &= cand - 1u;
+          const float4 p = s.bucket[warp][i];
+          const float d = point_dist2<D>(q, p.x, p.y, p.z);
+          nk = pack_key(d, __float_as_int(p.w));
+          take = d < kFar && nk < top.kth;
+        } while (!take && cand);
+        if (take) {
+          KNN_PF_CNT(11, 1);
+          top.insert(nk);
+          kth = key_dist(top.kth);
+        }
+      }
+    }
+    __syncwarp();
+    KNN_PF_LAP(4);
+  };
+
   // ---- Seeding. Each lane locates its query's Morton rank among the sorted
-  // leaves (binary search, leaf codes recomputed against the root box) and
-  // scores the `win` leaves around it. Near neighbours sit close to the query
-  // in Morton order, so this makes the k-th distance tight before the exact
-  // traversal starts; that traversal then skips the seeded window per lane.
-  // The window only affects speed: every seeded point is fully evaluated.
-  const int64_t win = n < int64_t(kSeedWindow * K) ? n : int64_t(kSeedWindow * K);
-  int64_t w0 = 0;
+  // leaves (binary search, leaf codes recomputed against the root box). Near
+  // neighbours sit close to the query in Morton order, so scoring the leaves
+  // around that rank makes the k-th distance tight before the exact traversal
+  // starts; the traversal then skips the seeded leaves. The seed only affects
+  // speed: every seeded point is fully evaluated.
+  int64_t rank = 0;
   if (mine) {
     const uint32_t qcode = morton_code<D>(q, root_lo, root_hi);
     int64_t lo = 0, hi = n;
@@ -385,33 +462,83 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
       load_leaf<D>(rows, leaf_row0 + mid, p);
       if (morton_code<D>(p, root_lo, root_hi) < qcode) lo = mid + 1; else hi = mid;
     }
-    w0 = lo - win / 2;
-    if (w0 > n - win) w0 = n - win;
-    if (w0 < 0) w0 = 0;
+    rank = lo;
   }
   KNN_PF_LAP(0);
-  const int64_t w1 = mine ? w0 + win : 0;
-  // The first K window points fill the list (only distances < FLT_MAX enter,
-  // as with insertions into an empty list), then the rest are offered.
-  if (mine) {
+  int64_t w0, w1;  // seeded leaves [w0, w1): the lane's own (per-lane window) or the warp's (union)
+  if constexpr (kUnionSeed) {
+    // The union of the lanes' windows: [min rank - K, max rank + K), at least
+    // K leaves, at most kUnionCap. Every lane scores every leaf of it, so a
+    // lane whose own window is poor (a Morton-cell boundary) borrows its
+    // neighbours' candidates. Staged 32 leaves at a time with coalesced loads;
+    // the first K fill every lane's list.
+    int64_t rmin = mine ? rank : n, rmax = mine ? rank : 0;
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      float p[D];
-      load_leaf<D>(rows, leaf_row0 + w0 + i, p);
-      const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      top.seed_slot(i, d < kFar ? pack_key(d, int32_t(sorted[w0 + i])) : kEmptyKey);
+    for (int o = 16; o > 0; o >>= 1) {
+      const int64_t a = __shfl_xor_sync(kFullMask, rmin, o);
+      const int64_t b = __shfl_xor_sync(kFullMask, rmax, o);
+      rmin = a < rmin ? a : rmin;
+      rmax = b > rmax ? b : rmax;
     }
-    top.seed_done();
-    kth = key_dist(top.kth);
+    w0 = rmin - K < 0 ? 0 : rmin - K;
+    w1 = rmax + K > n ? n : rmax + K;
+    if (w1 - w0 < K) {  // n >= K: widen to K leaves inside [0, n)
+      w1 = w0 + K > n ? n : w0 + K;
+      w0 = w1 - K;
+    }
+    if (w1 - w0 > kUnionCap) w1 = w0 + kUnionCap;
+    for (int64_t s0 = w0; s0 < w1; s0 += 32) {
+      const int cnt = int(w1 - s0 < 32 ? w1 - s0 : 32);
+      stage_leaves(s0, cnt);
+      int from = 0;
+      if (s0 == w0) {
+        if (mine) {
+          for (int i = 0; i < K; ++i) {
+            const float4 p = s.bucket[warp][i];
+            const float d = point_dist2<D>(q, p.x, p.y, p.z);
+            top.seed_slot(i, d < kFar ? pack_key(d, __float_as_int(p.w)) : kEmptyKey);
+          }
+          top.seed_done();
+          kth = key_dist(top.kth);
+        } else {
+          top.kth = 0ull;  // accepts nothing
+        }
+        from = K;
+      }
+      mark_and_insert(from, cnt, 0u);
+    }
   } else {
-    top.kth = 0ull;  // accepts nothing
-  }
-  for (int64_t i = K; i < win; ++i) {
+    // Each lane's own window of kSeedWindow * K leaves around its rank.
+    const int64_t win = n < int64_t(kSeedWindow * K) ? n : int64_t(kSeedWindow * K);
+    w0 = 0;
     if (mine) {
-      float p[D];
-      load_leaf<D>(rows, leaf_row0 + w0 + i, p);
-      const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
-      if (d < kFar) offer(pack_key(d, int32_t(sorted[w0 + i])));
+      w0 = rank - win / 2;
+      if (w0 > n - win) w0 = n - win;
+      if (w0 < 0) w0 = 0;
+    }
+    w1 = mine ? w0 + win : 0;
+    // The first K window points fill the list (only distances < FLT_MAX enter,
+    // as with insertions into an empty list), then the rest are offered.
+    if (mine) {
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        float p[D];
+        load_leaf<D>(rows, leaf_row0 + w0 + i, p);
+        const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
+        top.seed_slot(i, d < kFar ? pack_key(d, int32_t(sorted[w0 + i])) : kEmptyKey);
+      }
+      top.seed_done();
+      kth = key_dist(top.kth);
+    } else {
+      top.kth = 0ull;  // accepts nothing
+    }
+    for (int64_t i = K; i < win; ++i) {
+      if (mine) {
+        float p[D];
+        load_leaf<D>(rows, leaf_row0 + w0 + i, p);
+        const float d = point_dist2<D>(q, p[0], p[1], D == 3 ? p[2] : 0.0f);
+        if (d < kFar) offer(pack_key(d, int32_t(sorted[w0 + i])));
+      }
     }
   }
   __syncwarp();
@@ -429,56 +556,19 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
         const int64_t start = node << bucket_span;
         const int64_t rem = n - start;
         const int count = int(rem < (int64_t(1) << bucket_span) ? rem : (int64_t(1) << bucket_span));
-        if (int(lane) < count) {
-          float p[D];
-          load_leaf<D>(rows, leaf_row0 + start + lane, p);
-          const int32_t src = int32_t(sorted[start + lane]);
-          s.bucket[warp][lane] = make_float4(p[0], p[1], D == 3 ? p[2] : 0.0f, __int_as_float(src));
-        }
-        __syncwarp();
-        // Pass 1: every lane marks the points within its current k-th distance.
-        uint32_t cand = 0;
-        if (count == kBucketSize) {
-#pragma unroll
-          for (int i = 0; i < kBucketSize; ++i) {
-            const float4 p = s.bucket[warp][i];
-            if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
-          }
-        } else {
-          for (int i = 0; i < count; ++i) {
-            const float4 p = s.bucket[warp][i];
-            if (point_dist2<D>(q, p.x, p.y, p.z) <= kth) cand |= 1u << i;
-          }
-        }
-        // Points of this lane's seeded window were scored already.
+        stage_leaves(start, count);
+        // Points of the seeded range were scored already.
+        uint32_t skip = 0;
         const int64_t slo = w0 - start;
         const int64_t shi = w1 - start;
         if (shi > 0 && slo < count) {
           const int b0 = slo > 0 ? int(slo) : 0;
           const int b1 = shi < count ? int(shi) : count;
           const uint32_t upto = b1 >= 32 ? 0xffffffffu : ((1u << b1) - 1u);
-          cand &= ~(upto & ~((1u << b0) - 1u));
+          skip = upto & ~((1u << b0) - 1u);
         }
-        __syncwarp();
-        KNN_PF_LAP(3);
         KNN_PF_CNT(9, 1);
-        // Pass 2: insert the marked points, one per lane per round, so the warp
-        // pays max-over-lanes(marks) insertions per bucket.
-        while (__any_sync(kFullMask, cand != 0u)) {
-          KNN_PF_CNT(10, 1);
-          if (cand) {
-            const int i = __ffs(cand) - 1;
-            cand &= cand - 1u;
-            const float4 p = s.bucket[warp][i];
-            const float d = point_dist2<D>(q, p.x, p.y, p.z);
-#if TBVH_KNN_PROFILE
-            if (d < kFar && pack_key(d, __float_as_int(p.w)) < top.kth) KNN_PF_CNT(11, 1);
-#endif
-            if (d < kFar) offer(pack_key(d, __float_as_int(p.w)));
-          }
-        }
-        __syncwarp();
-        KNN_PF_LAP(4);
+        mark_and_insert(0, count, skip);
       } else if (kWideSteps && level + 2 <= Lb) {
         // Two levels at once: the node's four grandchildren are four consecutive
         // rows of the next-but-one level (the first is always real). A

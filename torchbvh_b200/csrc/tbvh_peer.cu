@@ -40,6 +40,24 @@ int peer_set_device(int device, const char* op) {
   return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
 }
 
+// The driver's cuMemGetAddressRange (base and size of the allocation that
+// contains a device pointer), fetched through the runtime so that the library
+// needs no link-time dependency on libcuda. Signature of the driver API:
+// CUresult cuMemGetAddressRange(CUdeviceptr* base, size_t* size, CUdeviceptr ptr).
+using AddressRangeFn = int (*)(unsigned long long*, size_t*, unsigned long long);
+
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &status) != cudaSuccess ||
+        status != cudaDriverEntryPointSuccess)
+      return AddressRangeFn(nullptr);
+    return reinterpret_cast<AddressRangeFn>(p);
+  }();
+  return fn;
+}
+
 }  // namespace
 
 extern "C" {
@@ -60,6 +78,20 @@ int tbvh_peer_alloc(int device, size_t bytes, void** out_ptr, void* out_handle) 
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, bytes);
   if (e != cudaSuccess) return peer_cuda_fail(e, op);
+  // Refuse to share a buffer that does not start its own allocation: the other
+  // ranks would map the allocation's start, not this pointer.
+  const AddressRangeFn range = address_range_fn();
+  if (range == nullptr) {
+    cudaFree(p);
+    return peer_fail(TBVH_ERR_CUDA, op, "cannot query allocation ranges (cuMemGetAddressRange unavailable)");
+  }
+  unsigned long long base = 0;
+  size_t extent = 0;
+  if (range(&base, &extent, reinterpret_cast<unsigned long long>(p)) != 0 ||
+      base != reinterpret_cast<unsigned long long>(p) || extent < bytes) {
+    cudaFree(p);
+    return peer_fail(TBVH_ERR_CUDA, op, "the buffer is not the base of its own allocation; refusing to share it");
+  }
   cudaIpcMemHandle_t h;
   e = cudaIpcGetMemHandle(&h, p);
   if (e != cudaSuccess) {
