@@ -884,6 +884,11 @@ def run_reference_cuda(args, world, rank, local):
 
 def main():
     args = parse_args()
+    # stdout carries the one result line only: whatever else writes to it
+    # (NCCL's version banner at process-group start, for one) goes to stderr.
+    sys.stdout.flush()
+    result_fd = os.dup(1)
+    os.dup2(2, 1)
     if args.warmup < 3 and args.impl == "b200":
         print("note: fewer than 3 warm-up steps; this run is not a reportable measurement", file=sys.stderr)
     world, rank, local = dist_setup(args) if args.impl != "reference" else (
@@ -898,7 +903,7 @@ def main():
         else:
             result = run_b200(args, world, rank, local)
         if rank == 0 and result is not None:
-            print(json.dumps(result), flush=True)
+            os.write(result_fd, (json.dumps(result) + "\n").encode())
     finally:
         if world > 1 and args.impl != "reference":
             import torch.distributed as dist

@@ -79,6 +79,10 @@ constexpr bool kStackBounds = TBVH_KNN_STACK_BOUNDS != 0;
 #endif
 constexpr int kSeedWindow = TBVH_KNN_SEED_WINDOW;
 static_assert(kSeedWindow >= 1, "the window must hold at least k leaves");
+#ifndef TBVH_KNN_SEED_ALIGN
+#define TBVH_KNN_SEED_ALIGN 0
+#endif
+constexpr bool kSeedAlign = TBVH_KNN_SEED_ALIGN != 0;
 // 1: the warp seeds every lane from the union of the lanes' windows (at most
 // kUnionCap leaves, staged through shared memory); 0: each lane its own window.
 // Measured on B200 (traversal ms, union / own window): c4 47.6 / 46.8, c2 1.96 /
@@ -177,7 +181,7 @@ struct TopK {
   u64 key[K];
   u64 kth;
 
-  __device__ __forceinline__ void init(u64* /*heap_lane*/) {
+  __device__ __forceinline__ void init(u64* /*warp_heap*/, unsigned /*lane*/) {
 #pragma unroll
     for (int i = 0; i < K; ++i) key[i] = kEmptyKey;
     kth = kEmptyKey;
@@ -226,16 +230,48 @@ struct TopK {
   }
 };
 
-// k >= 16: max-heap per lane in shared memory, slot s of the lane at
-// h[s * 32] (consecutive lanes in consecutive words, so a warp's accesses to
-// any mix of slots are free of bank conflicts beyond the 64-bit split).
+// Shared-memory word of slot s of lane l in a warp's heap area: row s, column
+// l, so lanes reach distinct banks whatever slots they touch (the sift-downs).
+// TBVH_KNN_SWIZZLE=1 uses column l XOR s instead, which makes the cooperative
+// row reads (lane s reads slot s of one lane) conflict-free but lets lanes
+// sifting different slots collide: c4 traversal 51.7 ms against 46.2 ms on
+// B200, so the plain layout is the default and the row reads take the
+// conflicts (one read per slot per row, once per query).
+#ifndef TBVH_KNN_SWIZZLE
+#define TBVH_KNN_SWIZZLE 0
+#endif
+// Cooperative row writes for heap top-k and the unrolled sift from the root
+// are on by default. c4 traversal on B200: both 46.2 ms, sift only 46.6 ms,
+// neither 46.9 ms (the writes matter more when rows go to peer GPUs).
+#ifndef TBVH_KNN_COOP_WRITE
+#define TBVH_KNN_COOP_WRITE 1
+#endif
+#ifndef TBVH_KNN_UNROLLED_SIFT
+#define TBVH_KNN_UNROLLED_SIFT 1
+#endif
+__device__ __forceinline__ int heap_word(int s, unsigned l) {
+  return TBVH_KNN_SWIZZLE ? s * 32 + int(l ^ unsigned(s & 31)) : s * 32 + int(l);
+}
+
+// k >= 16: max-heap per lane in shared memory (the warp's area, swizzled by
+// heap_word), heap-sorted in place at the end.
 template <int K>
 struct TopK<K, true> {
-  u64* h;
-  u64 kth;  // the root, h[0]
+  u64* hw;  // the warp's heap area
+  unsigned ln;
+  u64 kth;  // the root
 
-  __device__ __forceinline__ void init(u64* heap_lane) {
-    h = heap_lane;
+  struct Slots {
+    u64* hw;
+    unsigned ln;
+    __device__ __forceinline__ u64& operator[](int s) const { return hw[heap_word(s, ln)]; }
+  };
+  Slots h;
+
+  __device__ __forceinline__ void init(u64* warp_heap, unsigned lane) {
+    hw = warp_heap;
+    ln = lane;
+    h = Slots{warp_heap, lane};
     kth = kEmptyKey;
   }
   // Moves x down from slot i of a heap of n slots.
@@ -244,28 +280,58 @@ struct TopK<K, true> {
     for (;;) {
       int c = 2 * i + 1;
       if (c >= n) break;
-      u64 a = h[c * 32];
+      u64 a = h[c];
       if (c + 1 < n) {
-        const u64 b = h[(c + 1) * 32];
+        const u64 b = h[c + 1];
         if (b > a) {
           a = b;
           ++c;
         }
       }
       if (a <= x) break;
-      h[i * 32] = a;
+      h[i] = a;
       i = c;
     }
-    h[i * 32] = x;
+    h[i] = x;
   }
-  __device__ __forceinline__ void seed_slot(int i, u64 v) { h[i * 32] = v; }
+  __device__ __forceinline__ void seed_slot(int i, u64 v) { h[i] = v; }
   __device__ __forceinline__ void seed_done() {  // bottom-up heapify
 #pragma unroll 1
-    for (int i = K / 2 - 1; i >= 0; --i) sift_down(i, h[i * 32], K);
+    for (int i = K / 2 - 1; i >= 0; --i) sift_down(i, h[i], K);
     kth = h[0];
   }
   __device__ __forceinline__ void insert(u64 nk) {  // requires nk < kth: replaces the root
-    sift_down(0, nk, K);
+    if (!TBVH_KNN_UNROLLED_SIFT) {
+      sift_down(0, nk, K);
+      kth = h[0];
+      return;
+    }
+    // The sift from the root unrolled over the heap's log2(K) levels, both
+    // children loaded together at each level. The last internal slot (K/2 - 1)
+    // has only a left child; its missing right one reads as key 0, which never
+    // wins (keys are >= 0 and a move needs a child strictly above nk).
+    constexpr int kLevels = K >= 32 ? 5 : K >= 16 ? 4 : K >= 8 ? 3 : 2;
+    int i = 0;
+    bool moving = true;
+#pragma unroll
+    for (int lvl = 0; lvl < kLevels; ++lvl) {
+      const int c = 2 * i + 1;
+      if (moving && c < K) {
+        u64 a = h[c];
+        const u64 b = c + 1 < K ? h[c + 1] : 0ull;
+        const bool right = b > a;
+        a = right ? b : a;
+        if (a > nk) {
+          h[i] = a;
+          i = c + (right ? 1 : 0);
+        } else {
+          moving = false;
+        }
+      } else {
+        moving = false;
+      }
+    }
+    h[i] = nk;
     kth = h[0];
   }
   // In-place heap sort: slots end ascending.
@@ -273,12 +339,12 @@ struct TopK<K, true> {
 #pragma unroll 1
     for (int end = K - 1; end > 0; --end) {
       const u64 top = h[0];
-      const u64 last = h[end * 32];
-      h[end * 32] = top;
+      const u64 last = h[end];
+      h[end] = top;
       sift_down(0, last, end);
     }
   }
-  __device__ __forceinline__ u64 at(int i) const { return h[i * 32]; }
+  __device__ __forceinline__ u64 at(int i) const { return h[i]; }
 };
 
 template <int D>
@@ -315,6 +381,44 @@ __device__ __forceinline__ void write_row(const TopK<K, kHeap>& top, int64_t* oi
     reinterpret_cast<longlong2*>(oi)[i / 2] = make_longlong2(key_idx(k0), key_idx(k1));
     reinterpret_cast<longlong2*>(oi)[i / 2 + 1] = make_longlong2(key_idx(k2), key_idx(k3));
     reinterpret_cast<float4*>(od)[i / 4] = make_float4(key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
+  }
+}
+
+// Result rows of a warp whose heaps are sorted, written cooperatively: for each
+// lane j of `mask` (32 / K lanes per pass), lane s of the warp writes slot s of
+// j's row, so one row is a single contiguous 8·K-byte index store and a 4·K-byte
+// distance store (instead of 16-byte pieces of 32 scattered rows per warp
+// instruction). Row `row_of_lane` of lane j; every destination buffer when
+// kToDest (peer memory included), else out_idx / out_dist.
+template <int K, bool kToDest>
+__device__ __forceinline__ void write_rows_coop(const KnnArgs& a, const u64* hw, unsigned mask, int64_t row_of_lane,
+                                                unsigned lane) {
+  constexpr int kPerPass = 32 / K;
+  const int sub = int(lane) / K;
+  const int slot = int(lane) % K;
+  while (mask) {
+    int j = -1;
+#pragma unroll
+    for (int r = 0; r < kPerPass; ++r) {
+      const int next = mask ? __ffs(mask) - 1 : -1;
+      if (r == sub) j = next;
+      if (mask) mask &= mask - 1u;
+    }
+    const int64_t row = __shfl_sync(kFullMask, row_of_lane, j < 0 ? 0 : j);
+    if (j >= 0) {
+      const u64 key = hw[heap_word(slot, unsigned(j))];
+      const int64_t at = row * K + slot;
+      if constexpr (kToDest) {
+#pragma unroll 1
+        for (int dst = 0; dst < a.num_dest; ++dst) {
+          a.dest_idx[dst][at] = key_idx(key);
+          a.dest_dist[dst][at] = key_dist(key);
+        }
+      } else {
+        a.out_idx[at] = key_idx(key);
+        a.out_dist[at] = key_dist(key);
+      }
+    }
   }
 }
 
@@ -376,7 +480,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
   }
 
   TopK<K, kHeap> top;
-  top.init(kHeap ? &s.heap[kHeap ? warp : 0][0][lane] : nullptr);
+  top.init(kHeap ? &s.heap[kHeap ? warp : 0][0][0] : nullptr, lane);
   float kth = mine ? kFar : -1.0f;  // disabled lanes admit nothing
   // Offers a candidate key whose distance is already known to be < FLT_MAX.
   auto offer = [&](u64 nk) {
@@ -512,7 +616,9 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
     const int64_t win = n < int64_t(kSeedWindow * K) ? n : int64_t(kSeedWindow * K);
     w0 = 0;
     if (mine) {
-      w0 = rank - win / 2;
+      // Centred on the rank, or (TBVH_KNN_SEED_ALIGN) the aligned block of
+      // `win` leaves that holds it, which is one subtree of the implicit tree.
+      w0 = kSeedAlign ? rank / win * win : rank - win / 2;
       if (w0 > n - win) w0 = n - win;
       if (w0 < 0) w0 = 0;
     }
@@ -726,11 +832,32 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
   if (int(lane) == pf_leader) {
     for (int i = 0; i < 16; ++i) atomicAdd(&g_knn_profile[i], pf_[i]);
   }
+#else
+  if (mine) top.finish();
 #endif
+  if constexpr (kHeap && TBVH_KNN_COOP_WRITE) {
+    // Rows leave through the cooperative writer; result rows (and, over
+    // NVLink, the peers' copies) are then whole-row stores.
+    __syncwarp();
+    const int64_t row = kToDest ? gq : (a.spatial ? pos : gq);
+    write_rows_coop<K, kToDest>(a, top.hw, __ballot_sync(kFullMask, mine), row, lane);
+    if constexpr (!kToDest) {
+      if (mine && a.out_pos) {
+        // Fused source_points[indices] gather (see below for the rule on -1).
+        const float* src = a.src_points + pt_off * D;
+        float* op = a.out_pos + row * K * D;
+#pragma unroll 4
+        for (int i = 0; i < K; ++i) {
+          int64_t idx = key_idx(top.at(i));
+          if (idx < 0) idx = n - 1;
+#pragma unroll
+          for (int c = 0; c < D; ++c) op[i * D + c] = __ldg(src + idx * D + c);
+        }
+      }
+    }
+    return;
+  }
   if (!mine) return;
-#if !TBVH_KNN_PROFILE
-  top.finish();
-#endif
   if constexpr (kToDest) {
     // Result row delivered to every destination buffer at the query's row.
     // Destinations on other GPUs are written over NVLink as the results come
