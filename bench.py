@@ -494,11 +494,22 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
     # value: results all-gathered, the traversal delivering every row to every
     # rank's buffer over NVLink (PeerResults, reused across steps).
     gather_steps = max(3, min(args.steps, 10))
+    # Phase markers of the sharded call (events on the current stream), to
+    # split a rank's step into broadcast / build / share / traversal / delivery.
+    phase_events: list = []
+
+    def phase_hook(name, dev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        phase_events.append((name, ev))
+
     with tdist.PeerResults(m, k, device=device) as peer:
         _native._knn_hooks.append(hook)
+        tdist._phase_hooks.append(phase_hook)
         sampler = ClockSampler(local)
         with sampler:
             total_ms, launches = timed("all", args.steps, args.warmup, resident, peer)
+        tdist._phase_hooks.remove(phase_hook)
         _native._knn_hooks.remove(hook)
         total_ms_max = max_over_ranks(total_ms, world)
         starts = [e for ph, e in knn_events if ph == "start"][-args.steps:]
@@ -507,8 +518,14 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         knn_avg_ms = max_over_ranks(knn_local_ms, world)
         import torch.distributed as dist
 
+        order = ["start", "broadcast", "build", "share", "traversal", "delivered"]
+        steps_ev = [phase_events[i:i + len(order)] for i in range(0, len(phase_events), len(order))][-args.steps:]
+        phases = {}
+        for a_name, b_name in zip(order, order[1:]):
+            ia, ib = order.index(a_name), order.index(b_name)
+            phases[b_name + "_ms"] = sum(s[ia][1].elapsed_time(s[ib][1]) for s in steps_ev) / len(steps_ev)
         per_rank = [None] * world
-        dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps})
+        dist.all_gather_object(per_rank, {"knn_ms": knn_local_ms, "step_ms": total_ms / args.steps, **phases})
     inplace_ms = max_over_ranks(timed("none", gather_steps, 3, resident)[0], world)
     nccl_gather_ms = max_over_ranks(timed("all", gather_steps, 3, resident)[0], world)
     status = torchbvh.device_status(device)

@@ -225,6 +225,18 @@ int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sor
                          int dim, int k, int num_dest, int64_t* const* dest_indices,
                          float* const* dest_distances, void* stream);
 
+/* tbvh_query_knn_share with int32 destination index buffers ([num_queries, k]):
+ * 8 instead of 12 bytes per neighbour cross NVLink; every rank then widens its
+ * own buffer with tbvh_widen_indices (local HBM traffic). No reference
+ * counterpart. Point counts are below 2^31, so int32 holds every index (and -1). */
+int tbvh_query_knn_share_i32(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
+                             const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
+                             int dim, int k, int num_dest, int32_t* const* dest_indices,
+                             float* const* dest_distances, void* stream);
+
+/* dst[i] = src[i] (int32 -> int64) for i < count, on `stream`. No reference counterpart. */
+int tbvh_widen_indices(int device, const int32_t* src, int64_t* dst, int64_t count, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -147,3 +147,26 @@ def test_interleaved_share_matches_single_gpu_results():
     torch.cuda.synchronize()
     assert torch.equal(di, want_i) and torch.equal(dd, want_d)
     assert torchbvh.device_status() == 0
+
+
+@pytest.mark.parametrize("k", [8, 32])
+def test_int32_destinations_widen_to_the_int64_result(k):
+    """tbvh_query_knn_share_i32 + tbvh_widen_indices (the NVLink-thrifty form of the
+    fused all-gather) give the same rows as the int64 path (register and heap top-k)."""
+    points = _cloud(70, (30_000, 3))
+    queries = _cloud(71, (7_001, 3))
+    with torchbvh.BVH(points) as bvh:
+        want_i, want_d = bvh.knn(queries, k)
+        h = bvh._handle
+        order = _C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                              h["scene_max"].unsqueeze(0))[0].contiguous()
+        wire = [torch.full((7_001, k), -5, dtype=torch.int32, device="cuda") for _ in range(2)]
+        dd = [torch.full((7_001, k), -5.0, device="cuda") for _ in range(2)]
+        _native.query_knn_share(h["node_aabbs"], h["sorted_indices"], 30_000, queries, order, k,
+                                [w.data_ptr() for w in wire], [d.data_ptr() for d in dd], index_bits=32)
+        wide = torch.empty((7_001, k), dtype=torch.int64, device="cuda")
+        _native.widen_indices(wire[1], wide)
+    torch.cuda.synchronize()
+    assert torch.equal(wide, want_i) and torch.equal(dd[0], want_d) and torch.equal(dd[1], want_d)
+    assert torch.equal(wire[0].long(), want_i)
+    assert torchbvh.device_status() == 0

@@ -79,6 +79,12 @@ _SIGNATURES = {
         [_i32, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i32, _i32, _i32, ctypes.POINTER(_ptr),
          ctypes.POINTER(_ptr), _ptr],
     ),
+    "tbvh_query_knn_share_i32": (
+        _i32,
+        [_i32, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i32, _i32, _i32, ctypes.POINTER(_ptr),
+         ctypes.POINTER(_ptr), _ptr],
+    ),
+    "tbvh_widen_indices": (_i32, [_i32, _ptr, _ptr, _i64, _ptr]),
     "tbvh_query_knn_gather": (
         _i32,
         [_i32, _ptr, _ptr, _i64, _i64, _ptr, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i32, _i32, _ptr, _ptr, _ptr, _ptr,
@@ -526,11 +532,21 @@ def device_tensor(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.devi
         return torch.as_tensor(_DeviceView(ptr, shape, typestr), device=device)
 
 
+def widen_indices(src: torch.Tensor, dst: torch.Tensor) -> None:
+    """dst (int64) = src (int32), same number of elements, on the current stream."""
+    if not (src.is_cuda and dst.is_cuda and src.is_contiguous() and dst.is_contiguous()
+            and src.dtype == torch.int32 and dst.dtype == torch.int64 and src.numel() == dst.numel()):
+        raise RuntimeError("widen_indices: need contiguous CUDA int32 -> int64 tensors of equal size")
+    _check(load_library().tbvh_widen_indices(src.device.index, src.data_ptr(), dst.data_ptr(), src.numel(),
+                                             _stream(src.device)))
+
+
 def query_knn_share(node_aabbs: torch.Tensor, sorted_indices: torch.Tensor, num_points: int,
                     queries: torch.Tensor, share: torch.Tensor, k: int,
-                    dest_indices: list[int], dest_distances: list[int]) -> None:
+                    dest_indices: list[int], dest_distances: list[int], index_bits: int = 64) -> None:
     """k-NN of the queries listed in `share` (int64 indices into `queries`), each result
-    row written at the query's row of every destination buffer (tbvh_query_knn_share)."""
+    row written at the query's row of every destination buffer (tbvh_query_knn_share;
+    index_bits = 32: int32 destination index buffers, tbvh_query_knn_share_i32)."""
     op = "query_knn_share"
     if not (queries.is_cuda and queries.is_contiguous() and queries.dtype == torch.float32 and queries.dim() == 2):
         raise RuntimeError(f"{op}: queries must be contiguous CUDA float32 (M, D)")
@@ -547,7 +563,10 @@ def query_knn_share(node_aabbs: torch.Tensor, sorted_indices: torch.Tensor, num_
     if hooks:
         for h in hooks:
             h("start", device)
-    _check(lib.tbvh_query_knn_share(
+    if index_bits not in (32, 64):
+        raise RuntimeError(f"{op}: index_bits must be 32 or 64")
+    entry = lib.tbvh_query_knn_share_i32 if index_bits == 32 else lib.tbvh_query_knn_share
+    _check(entry(
         device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), int(num_points), queries.data_ptr(),
         int(queries.size(0)), share.data_ptr(), int(share.numel()), int(queries.size(1)), int(k), n_dest,
         idx_arr, dist_arr, _stream(device),

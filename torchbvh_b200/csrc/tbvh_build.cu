@@ -277,43 +277,57 @@ __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, Clo
   int cur = -1;
   int64_t cur_end = -1;
   float lo[D], hi[D];
-  for (int64_t r = 0; r < rounds; ++r) {
-    const int64_t i = (r * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
-    const bool valid = i < n;
-    uint32_t code = 0;
-    int c = 0;
-    if (valid) {
-      if (i >= cur_end || cur < 0) {
-        cur = cm.find(i);
-        cur_end = cm.start(cur) + cm.size(cur);
+  // Rounds go in groups of four whose points are all loaded before any is
+  // used, so each thread has four loads in flight instead of one.
+  constexpr int kGroup = 4;
+  for (int64_t r0 = 0; r0 < rounds; r0 += kGroup) {
+    float pg[kGroup][D];
 #pragma unroll
-        for (int a = 0; a < D; ++a) {
-          if (kEncodedBounds) {
-            lo[a] = ordered_to_float(enc[cur * 2 * D + a]);
-            hi[a] = ordered_to_float(enc[cur * 2 * D + D + a]);
-          } else {
-            lo[a] = smin[cur * D + a];
-            hi[a] = smax[cur * D + a];
+    for (int u = 0; u < kGroup; ++u) {
+      const int64_t i = ((r0 + u) * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
+      if (r0 + u < rounds && i < n) {
+#pragma unroll
+        for (int a = 0; a < D; ++a) pg[u][a] = __ldg(pts + i * D + a);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGroup; ++u) {
+      const int64_t r = r0 + u;
+      if (r >= rounds) break;  // uniform across the grid
+      const int64_t i = (r * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
+      const bool valid = i < n;
+      uint32_t code = 0;
+      int c = 0;
+      if (valid) {
+        if (i >= cur_end || cur < 0) {
+          cur = cm.find(i);
+          cur_end = cm.start(cur) + cm.size(cur);
+#pragma unroll
+          for (int a = 0; a < D; ++a) {
+            if (kEncodedBounds) {
+              lo[a] = ordered_to_float(enc[cur * 2 * D + a]);
+              hi[a] = ordered_to_float(enc[cur * 2 * D + D + a]);
+            } else {
+              lo[a] = smin[cur * D + a];
+              hi[a] = smax[cur * D + a];
+            }
           }
         }
+        c = cur;
+        code = morton_code<D>(pg[u], lo, hi);
+        keys[i] = code;
       }
-      c = cur;
-      float p[D];
-#pragma unroll
-      for (int a = 0; a < D; ++a) p[a] = pts[i * D + a];
-      code = morton_code<D>(p, lo, hi);
-      keys[i] = code;
-    }
-    // Digits of Morton codes in input order are mostly distinct within a warp,
-    // so each lane adds its own count; only a digit the whole warp shares (the
-    // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
-    for (int ps = 0; ps < passes; ++ps) {
-      const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
-      const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
-      if (__all_sync(kFullMask, d == d0)) {
-        if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);
-      } else if (d < 0x100u) {
-        atomicAdd(&s_hist[ps][d], 1u);
+      // Digits of Morton codes in input order are mostly distinct within a warp,
+      // so each lane adds its own count; only a digit the whole warp shares (the
+      // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
+      for (int ps = 0; ps < passes; ++ps) {
+        const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
+        const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
+        if (__all_sync(kFullMask, d == d0)) {
+          if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);
+        } else if (d < 0x100u) {
+          atomicAdd(&s_hist[ps][d], 1u);
+        }
       }
     }
   }
@@ -658,28 +672,41 @@ __global__ void __launch_bounds__(kTreeThreads) k_tree(TreeArgs a) {
   const int64_t limit = block_end < n ? block_end : n;
   auto present = [&](int level, int64_t j) { return (j << (L - level)) < limit; };
 
-  // Leaves: 4 consecutive sorted positions per thread.
+  // Leaves: 4 consecutive sorted positions per thread. All four indices are
+  // read, then all four points gathered, and only then are rows stored: the
+  // stores could alias the points as far as the compiler knows, so mixing them
+  // would serialise four round trips to DRAM per thread.
   float lo4[4][D], hi4[4][D];
+  int64_t src4[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int64_t pos = base + 4 * tid + q;
+    src4[q] = pos < limit ? __ldg(a.sorted + pt_off + pos) : -1;
+  }
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int64_t pos = base + 4 * tid + q;
     if (pos < limit) {
-      int64_t src = a.sorted[pt_off + pos];
+      int64_t src = src4[q];
       if (src < 0 || src >= n) {  // only reachable if the sort was corrupted; keep the read in bounds
         device_error(a.status, kDevErrBadIndex);
         src = 0;
       }
 #pragma unroll
       for (int c = 0; c < D; ++c) {
-        const float v = a.points[(pt_off + src) * D + c];
+        const float v = __ldg(a.points + (pt_off + src) * D + c);
         lo4[q][c] = v;
         hi4[q][c] = v;
       }
-      ctx.emit(L, pos, lo4[q], hi4[q]);
     } else {
 #pragma unroll
       for (int c = 0; c < D; ++c) { lo4[q][c] = INFINITY; hi4[q][c] = -INFINITY; }
     }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int64_t pos = base + 4 * tid + q;
+    if (pos < limit) ctx.emit(L, pos, lo4[q], hi4[q]);
   }
   // Level L-1: two nodes per thread.
   float lo[D], hi[D];

@@ -148,6 +148,7 @@ struct KnnLaunch {
   // out_idx/out_dist, when num_dest > 0. Destinations may be peer-mapped
   // buffers of other GPUs (NVLink stores).
   int num_dest = 0;
+  bool dest_idx32 = false;  // dest_idx buffers hold int32 indices (the caller widens them)
   int64_t* dest_idx[kMaxDest] = {};
   float* dest_dist[kMaxDest] = {};
 };

@@ -141,6 +141,7 @@ struct KnnArgs {
   float* out_pos;           // nullable: (rows, K, D) neighbour positions
   int spatial;              // 1: write row = sorted (Morton) position, else the query's own row
   int num_dest;             // > 0: rows go to dest_* (row = query index) instead of out_*
+  int dest_idx32;           // 1: dest_idx buffers hold int32 indices
   int64_t* dest_idx[kMaxDest];
   float* dest_dist[kMaxDest];
   unsigned* status;
@@ -411,7 +412,11 @@ __device__ __forceinline__ void write_rows_coop(const KnnArgs& a, const u64* hw,
       if constexpr (kToDest) {
 #pragma unroll 1
         for (int dst = 0; dst < a.num_dest; ++dst) {
-          a.dest_idx[dst][at] = key_idx(key);
+          if (a.dest_idx32) {
+            reinterpret_cast<int32_t*>(a.dest_idx[dst])[at] = key_idx(key);
+          } else {
+            a.dest_idx[dst][at] = key_idx(key);
+          }
           a.dest_dist[dst][at] = key_dist(key);
         }
       } else {
@@ -872,9 +877,14 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
       const float4 d4 = make_float4(key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
 #pragma unroll 1
       for (int dst = 0; dst < a.num_dest; ++dst) {
-        longlong2* oi = reinterpret_cast<longlong2*>(a.dest_idx[dst] + gq * K + i);
-        oi[0] = i01;
-        oi[1] = i23;
+        if (a.dest_idx32) {
+          *reinterpret_cast<int4*>(reinterpret_cast<int32_t*>(a.dest_idx[dst]) + gq * K + i) =
+              make_int4(key_idx(k0), key_idx(k1), key_idx(k2), key_idx(k3));
+        } else {
+          longlong2* oi = reinterpret_cast<longlong2*>(a.dest_idx[dst] + gq * K + i);
+          oi[0] = i01;
+          oi[1] = i23;
+        }
         *reinterpret_cast<float4*>(a.dest_dist[dst] + gq * K + i) = d4;
       }
     }
@@ -1011,6 +1021,7 @@ cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream) {
   a.out_pos = q.out_positions;
   a.spatial = q.spatial ? 1 : 0;
   a.num_dest = q.num_dest;
+  a.dest_idx32 = q.dest_idx32 ? 1 : 0;
   for (int i = 0; i < kMaxDest; ++i) {
     a.dest_idx[i] = q.dest_idx[i];
     a.dest_dist[i] = q.dest_dist[i];

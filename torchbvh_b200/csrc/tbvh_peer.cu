@@ -133,11 +133,16 @@ int tbvh_peer_close(int device, void* ptr) {
   return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
 }
 
-int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
-                         const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
-                         int dim, int k, int num_dest, int64_t* const* dest_indices,
-                         float* const* dest_distances, void* stream) {
-  const char* op = "query_knn_share";
+}  // extern "C"
+
+namespace {
+
+// tbvh_query_knn_share and tbvh_query_knn_share_i32: the destination index
+// buffers hold int64 or int32 values.
+int share_impl(const char* op, int device, const float* node_aabbs, const int64_t* sorted_indices,
+               int64_t num_points, const float* queries, int64_t num_queries, const int64_t* order,
+               int64_t share_count, int dim, int k, int num_dest, void* const* dest_indices,
+               float* const* dest_distances, bool idx32, void* stream) {
   tbvh::record_error(TBVH_OK, "");
   if (dim != 2 && dim != 3) return peer_fail(TBVH_ERR_BAD_ARG, op, "D must be 2 or 3");
   if (k != 4 && k != 8 && k != 16 && k != 32)
@@ -178,11 +183,69 @@ int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sor
   q.dim = dim;
   q.k = k;
   q.num_dest = num_dest;
+  q.dest_idx32 = idx32;
   for (int i = 0; i < num_dest; ++i) {
-    q.dest_idx[i] = dest_indices[i];
+    q.dest_idx[i] = static_cast<int64_t*>(dest_indices[i]);
     q.dest_dist[i] = dest_distances[i];
   }
   const cudaError_t e = tbvh::launch_knn(q, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
+}
+
+// int32 -> int64, four values per thread when both ends are 16-byte aligned.
+__global__ void __launch_bounds__(256) k_widen_i32(const int32_t* __restrict__ src, int64_t* __restrict__ dst,
+                                                   int64_t count) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t quads = count / 4;
+  const bool aligned = (reinterpret_cast<uintptr_t>(src) % 16 == 0) && (reinterpret_cast<uintptr_t>(dst) % 16 == 0);
+  int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (aligned) {
+    for (int64_t g = i; g < quads; g += stride) {
+      const int4 v = reinterpret_cast<const int4*>(src)[g];
+      reinterpret_cast<longlong2*>(dst)[2 * g] = make_longlong2(v.x, v.y);
+      reinterpret_cast<longlong2*>(dst)[2 * g + 1] = make_longlong2(v.z, v.w);
+    }
+    for (int64_t j = quads * 4 + i; j < count; j += stride) dst[j] = src[j];
+  } else {
+    for (int64_t j = i; j < count; j += stride) dst[j] = src[j];
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int tbvh_query_knn_share(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
+                         const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
+                         int dim, int k, int num_dest, int64_t* const* dest_indices,
+                         float* const* dest_distances, void* stream) {
+  return share_impl("query_knn_share", device, node_aabbs, sorted_indices, num_points, queries, num_queries, order,
+                    share_count, dim, k, num_dest, reinterpret_cast<void* const*>(dest_indices), dest_distances,
+                    false, stream);
+}
+
+int tbvh_query_knn_share_i32(int device, const float* node_aabbs, const int64_t* sorted_indices, int64_t num_points,
+                             const float* queries, int64_t num_queries, const int64_t* order, int64_t share_count,
+                             int dim, int k, int num_dest, int32_t* const* dest_indices,
+                             float* const* dest_distances, void* stream) {
+  return share_impl("query_knn_share_i32", device, node_aabbs, sorted_indices, num_points, queries, num_queries,
+                    order, share_count, dim, k, num_dest, reinterpret_cast<void* const*>(dest_indices),
+                    dest_distances, true, stream);
+}
+
+int tbvh_widen_indices(int device, const int32_t* src, int64_t* dst, int64_t count, void* stream) {
+  const char* op = "widen_indices";
+  tbvh::record_error(TBVH_OK, "");
+  if (count < 0 || (count > 0 && (!src || !dst))) return peer_fail(TBVH_ERR_BAD_ARG, op, "bad arguments");
+  if (count == 0) return TBVH_OK;
+  int rc = peer_set_device(device, op);
+  if (rc) return rc;
+  int64_t blocks = (count / 4 + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  k_widen_i32<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, dst, count);
+  tbvh::count_launches(1);
+  const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TBVH_OK : peer_cuda_fail(e, op);
 }
 

@@ -81,6 +81,16 @@ def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Ten
 
 
 SPLITS = ("morton", "interleaved", "contiguous")
+
+# Optional observers of the phases of one sharded single-cloud call, each
+# called as hook(phase, device) on the host as the phase's work is enqueued
+# (bench.py records CUDA events there). Empty by default.
+_phase_hooks: list = []
+
+
+def _phase(name: str, device) -> None:
+    for hook in _phase_hooks:
+        hook(name, device)
 _RUNS_PER_RANK = 32  # ownership runs per rank of the interleaved split
 
 
@@ -128,18 +138,27 @@ class PeerResults:
     on other streams must be ordered before the next call by the caller.
     Create once, reuse across calls, ``close()`` on every rank together (a
     collective).
+
+    ``index_bits=32`` (default): indices cross NVLink as int32 (8 instead of 12
+    bytes per neighbour; point counts are below 2^31) into a shared int32
+    buffer, and each rank widens its copy into the int64 ``indices`` tensor
+    after the rows have arrived. ``index_bits=64`` writes int64 directly.
     """
 
-    def __init__(self, num_queries: int, k: int, *, group=None, device: torch.device | None = None):
+    def __init__(self, num_queries: int, k: int, *, group=None, device: torch.device | None = None,
+                 index_bits: int = 32):
         from . import _native
 
+        if index_bits not in (32, 64):
+            raise ValueError("PeerResults: index_bits must be 32 or 64")
         self.group = group
         self.world, self.rank = _world(group)
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.num_queries, self.k = int(num_queries), int(k)
+        self.index_bits = index_bits
         dev = self.device.index
         rows = max(self.num_queries, 1) * self.k
-        self._own = [_native.peer_alloc(dev, rows * 8), _native.peer_alloc(dev, rows * 4)]
+        self._own = [_native.peer_alloc(dev, rows * index_bits // 8), _native.peer_alloc(dev, rows * 4)]
         handles = [None] * self.world
         dist.all_gather_object(handles, (self._own[0][1], self._own[1][1]), group=group)
         self._opened: list[int] = []
@@ -155,7 +174,12 @@ class PeerResults:
             self.dest_indices.append(pi)
             self.dest_distances.append(pd)
         shape = (self.num_queries, self.k)
-        self.indices = _native.device_tensor(self._own[0][0], shape, torch.int64, self.device)
+        if index_bits == 64:
+            self.indices = _native.device_tensor(self._own[0][0], shape, torch.int64, self.device)
+            self._wire_indices = None
+        else:
+            self._wire_indices = _native.device_tensor(self._own[0][0], shape, torch.int32, self.device)
+            self.indices = torch.empty(shape, dtype=torch.int64, device=self.device)
         self.distances = _native.device_tensor(self._own[1][0], shape, torch.float32, self.device)
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.closed = False
@@ -164,6 +188,13 @@ class PeerResults:
         """Collective on the current stream after the writing launches: once it
         completes on a rank, every peer's rows have arrived in its buffers."""
         dist.all_reduce(self._flag, group=self.group)
+
+    def _widen(self) -> None:
+        """int32 wire indices -> this rank's int64 ``indices`` (after delivered())."""
+        if self._wire_indices is not None:
+            from . import _native
+
+            _native.widen_indices(self._wire_indices, self.indices)
 
     def close(self) -> None:
         from . import _native
@@ -177,7 +208,7 @@ class PeerResults:
         dist.barrier(group=self.group)
         for p, _ in self._own:
             _native.peer_free(self.device.index, p)
-        self.indices = self.distances = None
+        self.indices = self.distances = self._wire_indices = None
         self.closed = True
 
     def __enter__(self) -> "PeerResults":
@@ -196,14 +227,19 @@ def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, rank: i
 
     with BVH(points) as bvh:
         h = bvh._handle
+        _phase("build", queries.device)
         share = _owned_queries_cuda(h, queries, rank, world, split)
         # No rank may store into a peer's buffers while that peer still reads the
         # previous call's rows: a collective on every rank's current stream, after
         # its earlier reads and before any traversal, orders them.
         out.delivered()
+        _phase("share", queries.device)
         query_knn_share(h["node_aabbs"], h["sorted_indices"], points.shape[0], queries, share, k,
-                        out.dest_indices, out.dest_distances)
+                        out.dest_indices, out.dest_distances, index_bits=out.index_bits)
+    _phase("traversal", queries.device)
     out.delivered()
+    out._widen()
+    _phase("delivered", queries.device)
     return out.indices, out.distances
 
 
@@ -245,7 +281,9 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
     dev = device or queries.device
     buf = points if rank == src else torch.empty((num_points, dim), dtype=torch.float32, device=dev)
     buf = buf.contiguous()
+    _phase("start", dev)
     dist.broadcast(buf, src=src, group=group)
+    _phase("broadcast", dev)
     m = queries.shape[0]
     q0, q1 = shard_range(m, world, rank)
     queries = queries.contiguous()
