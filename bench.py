@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--c4-points", type=int, default=16_777_216,
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
+    ap.add_argument("--c4-index-bits", type=int, default=32, choices=[32, 64],
+                    help="c4 on N > 1 GPUs: width of the indices the traversal sends over NVLink")
     ap.add_argument("--c4-split", default="morton", choices=["morton", "interleaved", "contiguous"],
                     help="c4 on N > 1 GPUs: share of the queries per rank (one range of their Morton order, "
                          "runs of it dealt to the ranks in turn, or a range of their given order)")
@@ -503,7 +505,7 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         ev.record(torch.cuda.current_stream(dev))
         phase_events.append((name, ev))
 
-    with tdist.PeerResults(m, k, device=device) as peer:
+    with tdist.PeerResults(m, k, device=device, index_bits=args.c4_index_bits) as peer:
         _native._knn_hooks.append(hook)
         tdist._phase_hooks.append(phase_hook)
         sampler = ClockSampler(local)
