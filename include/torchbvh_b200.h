@@ -141,6 +141,12 @@ int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clou
  * Outputs: out_indices int64 [total_queries, k] (local source indices),
  * out_distances float32 [total_queries, k], ascending, at the query's row.
  * k in {4, 8, 16, 32}; every cloud must hold at least k points.
+ * The outputs (and out_positions below) may be memory of `device` or
+ * page-locked host memory (cudaHostAlloc / cudaHostRegister, mapped at the
+ * same address): the kernel then stores the finished rows across PCIe as it
+ * goes, and they are readable on the host once the stream has passed the
+ * call. Any other output pointer (pageable host memory, another device's
+ * memory) returns TBVH_ERR_BAD_ARG before a launch.
  */
 size_t tbvh_query_knn_workspace_size(int64_t num_clouds, int64_t points_per_cloud);
 int tbvh_query_knn(int device, const float* node_aabbs, const int64_t* sorted_indices,

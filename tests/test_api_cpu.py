@@ -169,3 +169,34 @@ def test_bvh_class_is_not_a_mapping():
     assert not hasattr(torchbvh.BVH, "__getitem__")
     for method in ("knn", "destroy", "__enter__", "__exit__"):
         assert callable(getattr(torchbvh.BVH, method))
+
+
+def test_out_pair_checks_on_cpu():
+    """``knn(..., out=...)`` argument rules (checked before any device work)."""
+    from torchbvh_b200._query import _checked_out
+
+    dev = torch.device("cuda", 0)
+    assert _checked_out(None, (5, 4), dev, None) is None
+    cpu_pair = (torch.empty((5, 4), dtype=torch.int64), torch.empty((5, 4)))
+    with pytest.raises(ValueError, match="pinned host memory"):
+        _checked_out(cpu_pair, (5, 4), dev, None)
+    with pytest.raises(ValueError, match="must be a pair"):
+        _checked_out(cpu_pair[0], (5, 4), dev, None)
+    with pytest.raises(ValueError, match="shape"):
+        _checked_out(cpu_pair, (5, 8), dev, None)
+    with pytest.raises(ValueError, match="indices must be a torch.int64"):
+        _checked_out((cpu_pair[1], cpu_pair[1]), (5, 4), dev, None)
+    with pytest.raises(ValueError, match="contiguous"):
+        _checked_out((torch.empty((4, 5), dtype=torch.int64).t(), cpu_pair[1]), (5, 4), dev, None)
+    with pytest.raises(ValueError, match="source_points"):
+        _checked_out(cpu_pair, (5, 4), dev, torch.zeros(1))
+
+
+def test_shared_buffer_views_cover_every_wire_dtype():
+    """PeerResults views its IPC buffers as int64 / int32 indices and float32
+    distances; each needs an array-interface type string of the right width."""
+    from torchbvh_b200 import _native
+
+    for dtype in (torch.int64, torch.int32, torch.float32):
+        typestr = _native._TYPESTR[dtype]
+        assert int(typestr[2:]) == torch.empty((), dtype=dtype).element_size()

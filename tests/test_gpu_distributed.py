@@ -1,7 +1,9 @@
-"""The multi-GPU layer on real GPUs: NCCL process groups of 2 ranks (one per
-GPU) running the sharded k-NN forms with the CUDA path, compared with the
-single-GPU result. Skipped on machines with fewer than 2 GPUs. NVLS is
-switched off and each group has a short timeout."""
+"""The multi-GPU layer on real GPUs: NCCL process groups of 1 and 2 ranks (one
+per GPU) running the sharded k-NN forms with the CUDA path, compared with the
+single-GPU result. The 1-rank group runs on any GPU box (it still goes through
+the IPC-shared result buffers and both index widths); the 2-rank group is
+skipped on machines with fewer than 2 GPUs. NVLS is switched off and each group
+has a short timeout."""
 
 from __future__ import annotations
 
@@ -73,15 +75,17 @@ def _worker(rank, world, port, outdir):
         i, d, rows = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, big_q.to(dev), 32,
                                                     num_points=big_p.shape[0], dim=3, device=dev, gather="none")
         out["single_none"] = (i.cpu(), d.cpu(), rows.cpu())
-        # Fused all-gather: each rank's traversal writes its rows into both
-        # ranks' buffers over NVLink; the same buffers serve consecutive calls.
-        peer = tdist.PeerResults(big_q.shape[0], 32, device=dev)
-        for rep, (split, qset) in enumerate(zip(("morton", "morton", "contiguous"), _peer_query_sets(big_q))):
-            i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, qset.to(dev), 32,
-                                                  num_points=big_p.shape[0], dim=3, device=dev, split=split,
-                                                  out=peer)
-            out[f"peer{rep}"] = (i.cpu().clone(), d.cpu().clone())
-        peer.close()
+        # Fused all-gather: each rank's traversal writes its rows into every
+        # rank's buffers over NVLink (int32 or int64 indices on the wire); the
+        # same buffers serve consecutive calls.
+        for bits in (32, 64):
+            peer = tdist.PeerResults(big_q.shape[0], 32, device=dev, index_bits=bits)
+            for rep, (split, qset) in enumerate(zip(("morton", "morton", "contiguous"), _peer_query_sets(big_q))):
+                i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, qset.to(dev), 32,
+                                                      num_points=big_p.shape[0], dim=3, device=dev, split=split,
+                                                      out=peer)
+                out[f"peer{bits}_{rep}"] = (i.cpu().clone(), d.cpu().clone())
+            peer.close()
         i, d = tdist.knn_sharded_batched(bp.to(dev), bq.to(dev), 8)
         out["batched"] = (i.cpu(), d.cpu())
         i, d = tdist.knn_sharded_ragged(rp.to(dev), bo, rq.to(dev), qo, 16)
@@ -93,15 +97,16 @@ def _worker(rank, world, port, outdir):
         (Path(outdir) / f"rank{rank}.err").write_text(traceback.format_exc())
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [1, pytest.param(2, marks=pytest.mark.skipif(
+    torch.cuda.device_count() < 2, reason="needs 2 GPUs"))])
 @pytest.mark.timeout(600)
-def test_sharded_knn_on_two_gpus_matches_one_gpu():
+def test_sharded_knn_matches_one_gpu(world):
     import torchbvh_b200 as torchbvh
 
     outdir = tempfile.mkdtemp()
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, outdir)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, outdir)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -123,18 +128,20 @@ def test_sharded_knn_on_two_gpus_matches_one_gpu():
     qot = torch.tensor(qo, device=dev)
     with torchbvh.BVH(rp.to(dev), batch_offsets=bot) as bvh:
         ri, rd = bvh.knn(rq.to(dev), 16, query_offsets=qot)
-    for r in range(2):
+    for r in range(world):
         got = torch.load(Path(outdir) / f"rank{r}.pt")
         assert torch.equal(got["single"][0], si.cpu()) and torch.equal(got["single"][1], sd.cpu())
         assert torch.equal(got["single_contiguous"][0], si.cpu())
         assert torch.equal(got["single_contiguous"][1], sd.cpu())
         i, d, rows = got["single_none"]
         assert torch.equal(i, si.cpu()[rows]) and torch.equal(d, sd.cpu()[rows])
-        for rep in range(3):
-            wi, wd = peer_want[rep]
-            assert torch.equal(got[f"peer{rep}"][0], wi) and torch.equal(got[f"peer{rep}"][1], wd)
+        for bits in (32, 64):
+            for rep in range(3):
+                wi, wd = peer_want[rep]
+                gi, gd = got[f"peer{bits}_{rep}"]
+                assert torch.equal(gi, wi) and torch.equal(gd, wd)
         assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
         assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())
-    shares = [torch.load(Path(outdir) / f"rank{r}.pt")["single_none"][2] for r in range(2)]
+    shares = [torch.load(Path(outdir) / f"rank{r}.pt")["single_none"][2] for r in range(world)]
     owned = torch.cat(shares)
     assert torch.equal(torch.sort(owned).values, torch.arange(big_q.shape[0]))

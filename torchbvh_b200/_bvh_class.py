@@ -41,14 +41,16 @@ class BVH:
         return self._handle.destroyed
 
     def knn(self, query_points: torch.Tensor, k: int, *, query_offsets: torch.Tensor | None = None,
-            source_points: torch.Tensor | None = None, sort_queries: bool = True):
+            source_points: torch.Tensor | None = None, sort_queries: bool = True, out=None):
         """Query k nearest neighbors (see ``query_knn``).
 
         For ragged BVHs ``query_offsets`` is required. For single/batched BVHs
         ``sort_queries`` controls Morton-sorted traversal (default True).
+        ``out=(indices, squared_distances)``: caller-owned result tensors on the
+        BVH's device or in pinned host memory (filled by the traversal itself).
         """
         return query_knn(self._handle, query_points, k, query_offsets=query_offsets, source_points=source_points,
-                         sort_queries=sort_queries)
+                         sort_queries=sort_queries, out=out)
 
     def destroy(self) -> None:
         destroy_bvh(self._handle)

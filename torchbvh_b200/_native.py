@@ -354,8 +354,26 @@ def morton_sort_queries_ragged(queries: torch.Tensor, query_offsets: torch.Tenso
 # k-NN
 # ---------------------------------------------------------------------------
 
+def _result_pair(op: str, out, shape: tuple, device: torch.device):
+    """The (indices, distances) the kernel writes: new tensors on ``device``, or the
+    caller's ``out`` pair (int64 / float32, contiguous, ``shape``), each on
+    ``device`` or in pinned host memory, which the kernel fills across PCIe."""
+    if out is None:
+        return (torch.empty(shape, dtype=torch.int64, device=device),
+                torch.empty(shape, dtype=torch.float32, device=device))
+    if not (isinstance(out, (tuple, list)) and len(out) == 2):
+        raise RuntimeError(f"{op}: out must be a pair (indices, distances)")
+    for t, dtype in zip(out, (torch.int64, torch.float32)):
+        if not (isinstance(t, torch.Tensor) and t.dtype == dtype and tuple(t.shape) == tuple(shape)
+                and t.is_contiguous()):
+            raise RuntimeError(f"{op}: out tensors must be contiguous int64 / float32 of shape {tuple(shape)}")
+        if not (t.device == device or (t.device.type == "cpu" and t.is_pinned())):
+            raise RuntimeError(f"{op}: out tensors must be on {device} or in pinned host memory")
+    return out[0], out[1]
+
+
 def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_leaves, num_real_nodes, dim, k,
-                source_points=None, spatial=False):
+                source_points=None, spatial=False, out=None):
     if dim not in (2, 3):
         raise RuntimeError(f"{op}: D must be 2 or 3")
     if not (query_points.is_cuda and query_points.is_contiguous() and query_points.dtype == torch.float32):
@@ -394,8 +412,7 @@ def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_l
                 and source_points.device == device):
             raise RuntimeError(f"{op}: source_points must be contiguous CUDA float32 of shape (B, N, D)")
     batch, m = int(query_points.size(0)), int(query_points.size(1))
-    indices = torch.empty((batch, m, k), dtype=torch.int64, device=device)
-    distances = torch.empty((batch, m, k), dtype=torch.float32, device=device)
+    indices, distances = _result_pair(op, out, (batch, m, k), device)
     positions = (torch.empty((batch, m, k, dim), dtype=torch.float32, device=device)
                  if source_points is not None else None)
     if batch * m == 0:
@@ -420,17 +437,19 @@ def _query_impl(op, node_aabbs, sorted_indices, query_points, query_order, num_l
     return (indices, distances) if positions is None else (indices, distances, positions)
 
 
-def query_knn_batched_cached_bounds(node_aabbs, sorted_indices, query_points, num_leaves, num_real_nodes, dim, k):
-    """Unordered exact k-NN (knn_query.cu:419-431)."""
+def query_knn_batched_cached_bounds(node_aabbs, sorted_indices, query_points, num_leaves, num_real_nodes, dim, k,
+                                    *, out=None):
+    """Unordered exact k-NN (knn_query.cu:419-431). ``out``: optional (B, M, k)
+    result pair to write into (see ``_result_pair``)."""
     return _query_impl("query_knn_batched_cached_bounds", node_aabbs, sorted_indices, query_points, None,
-                       num_leaves, num_real_nodes, dim, k)
+                       num_leaves, num_real_nodes, dim, k, out=out)
 
 
 def query_knn_batched_cached_bounds_ordered(node_aabbs, sorted_indices, query_points, query_order,
-                                            num_leaves, num_real_nodes, dim, k):
+                                            num_leaves, num_real_nodes, dim, k, *, out=None):
     """Morton-ordered exact k-NN (knn_query.cu:433-446); outputs in original query order."""
     return _query_impl("query_knn_batched_cached_bounds_ordered", node_aabbs, sorted_indices, query_points,
-                       query_order, num_leaves, num_real_nodes, dim, k)
+                       query_order, num_leaves, num_real_nodes, dim, k, out=out)
 
 
 def query_knn_batched_cached_bounds_spatial(node_aabbs, sorted_indices, query_points, query_order,
@@ -453,13 +472,12 @@ def query_knn_gather_positions(node_aabbs, sorted_indices, query_points, query_o
 
 
 def query_knn_ragged(packed: dict, query_points: torch.Tensor, query_offsets: torch.Tensor, total_queries: int,
-                     order: torch.Tensor | None, k: int, source_points: torch.Tensor | None = None):
+                     order: torch.Tensor | None, k: int, source_points: torch.Tensor | None = None, *, out=None):
     """Packed ragged exact k-NN over every cloud in one launch (no reference counterpart)."""
     dim = int(packed["dim"])
     device = query_points.device
     clouds = len(packed["point_offsets"]) - 1
-    indices = torch.empty((total_queries, k), dtype=torch.int64, device=device)
-    distances = torch.empty((total_queries, k), dtype=torch.float32, device=device)
+    indices, distances = _result_pair("query_knn_ragged", out, (total_queries, k), device)
     positions = (torch.empty((total_queries, k, dim), dtype=torch.float32, device=device)
                  if source_points is not None else None)
     if total_queries == 0:
@@ -525,9 +543,13 @@ class _DeviceView:
                                          "version": 3, "strides": None}
 
 
+# Array-interface type strings of the dtypes a shared buffer can hold.
+_TYPESTR = {torch.int64: "<i8", torch.int32: "<i4", torch.float32: "<f4"}
+
+
 def device_tensor(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
     """Tensor over memory this module owns (no copy; the owner must outlive it)."""
-    typestr = {torch.int64: "<i8", torch.float32: "<f4"}[dtype]
+    typestr = _TYPESTR[dtype]
     with torch.cuda.device(device):
         return torch.as_tensor(_DeviceView(ptr, shape, typestr), device=device)
 

@@ -216,8 +216,29 @@ def _checked_queries(layout: str, data: Mapping, query_points: torch.Tensor, dev
     return _as_contiguous(query_points)
 
 
+def _checked_out(out, shape: tuple, device: torch.device, source: torch.Tensor | None):
+    """``out=(indices, squared_distances)``: caller-owned result tensors of the
+    call's result shape (int64 / float32, contiguous), on the BVH's device or in
+    pinned host memory. With pinned host tensors the traversal stores each
+    finished row across PCIe as it goes (no device copy, no separate transfer);
+    they are complete once the current stream has passed the call."""
+    if out is None:
+        return None
+    _reject_unless(source is None, "query_knn: out cannot be combined with source_points")
+    _reject_unless(isinstance(out, (tuple, list)) and len(out) == 2,
+                   "query_knn: out must be a pair (indices, squared_distances)")
+    for t, dtype, name in zip(out, (torch.int64, torch.float32), ("indices", "squared_distances")):
+        _reject_unless(isinstance(t, torch.Tensor) and t.dtype == dtype,
+                       f"query_knn: out {name} must be a {dtype} tensor")
+        _reject_unless(tuple(t.shape) == tuple(shape), f"query_knn: out {name} must have shape {tuple(shape)}")
+        _reject_unless(t.is_contiguous(), f"query_knn: out {name} must be contiguous")
+        _reject_unless(t.device == device or (t.device.type == "cpu" and t.is_pinned()),
+                       "query_knn: out tensors must be on the BVH's device or in pinned host memory")
+    return tuple(out)
+
+
 def _run_fixed_size(data: Mapping, queries: torch.Tensor, k: int, source: torch.Tensor | None, sort_queries: bool,
-                    squeeze: bool):
+                    squeeze: bool, out=None):
     """Single clouds (as B = 1) and fixed-size batches: Morton order of the
     queries against each cloud's scene box, then the traversal."""
     lift = (lambda t: t.unsqueeze(0)) if squeeze else (lambda t: t)
@@ -234,37 +255,44 @@ def _run_fixed_size(data: Mapping, queries: torch.Tensor, k: int, source: torch.
         if squeeze:
             idx, dist, pos = idx[0], dist[0], pos[0]
         return idx, dist, _with_source_grad(source, pos, idx, n, base)
+    out_b = tuple(lift(t) for t in out) if out is not None else None
     if sort_queries:
-        idx, dist = _C.query_knn_batched_cached_bounds_ordered(*tree, queries_b, order, *sizes)
+        idx, dist = _C.query_knn_batched_cached_bounds_ordered(*tree, queries_b, order, *sizes, out=out_b)
     else:
-        idx, dist = _C.query_knn_batched_cached_bounds(*tree, queries_b, *sizes)
+        idx, dist = _C.query_knn_batched_cached_bounds(*tree, queries_b, *sizes, out=out_b)
+    if out is not None:
+        return out
     return (idx[0], dist[0]) if squeeze else (idx, dist)
 
 
 def _query_knn_single(bvh: BVHHandle, query_points: torch.Tensor, k: int, *,
-                      source_points: torch.Tensor | None = None, sort_queries: bool = True):
+                      source_points: torch.Tensor | None = None, sort_queries: bool = True, out=None):
     _validate_supported_k("query_knn", k)
     data = _bvh_data(bvh, "query_knn")
-    queries = _checked_queries(_SINGLE, data, query_points, data["sorted_indices"].device)
+    device = data["sorted_indices"].device
+    queries = _checked_queries(_SINGLE, data, query_points, device)
     if source_points is not None:
         source_points = _check_source_points(_SINGLE, "query_knn", source_points, data["num_leaves"], None,
-                                             data["dim"], data["sorted_indices"].device)
-    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=True)
+                                             data["dim"], device)
+    out = _checked_out(out, (queries.size(0), k), device, source_points)
+    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=True, out=out)
 
 
 def _query_knn_batched(bvh: BatchedBVHHandle, query_points: torch.Tensor, k: int, *,
-                       source_points: torch.Tensor | None = None, sort_queries: bool = True):
+                       source_points: torch.Tensor | None = None, sort_queries: bool = True, out=None):
     _validate_supported_k("query_knn", k)
     data = _batched_bvh_data(bvh, "query_knn")
-    queries = _checked_queries(_BATCHED, data, query_points, data["sorted_indices"].device)
+    device = data["sorted_indices"].device
+    queries = _checked_queries(_BATCHED, data, query_points, device)
     if source_points is not None:
         source_points = _check_source_points(_BATCHED, "query_knn", source_points, data["num_leaves"],
-                                             data["batch_size"], data["dim"], data["sorted_indices"].device)
-    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=False)
+                                             data["batch_size"], data["dim"], device)
+    out = _checked_out(out, (queries.size(0), queries.size(1), k), device, source_points)
+    return _run_fixed_size(data, queries, k, source_points, sort_queries, squeeze=False, out=out)
 
 
 def _query_knn_ragged(bvh: RaggedBVHHandle, query_points: torch.Tensor, query_offsets: torch.Tensor, k: int, *,
-                      source_points: torch.Tensor | None = None):
+                      source_points: torch.Tensor | None = None, out=None):
     _validate_supported_k("query_knn", k)
     data, packed = _ragged_bvh_data(bvh, "query_knn")
     device = data["batch_offsets"].device
@@ -280,9 +308,10 @@ def _query_knn_ragged(bvh: RaggedBVHHandle, query_points: torch.Tensor, query_of
         source_points = _check_source_points(_RAGGED, "query_knn", source_points, p_offsets[-1], None, data["dim"],
                                              device)
     total = q_offsets[-1]
+    out = _checked_out(out, (total, k), device, source_points)
     order = _C.morton_sort_queries_ragged(queries, query_offsets, total, packed["scene_min"], packed["scene_max"])
     if source_points is None:
-        return _C.query_knn_ragged(packed, queries, query_offsets, total, order, k)
+        return _C.query_knn_ragged(packed, queries, query_offsets, total, order, k, out=out)
     idx, dist, pos = _C.query_knn_ragged(packed, queries, query_offsets, total, order, k,
                                          source_points=source_points.detach())
     if torch.is_grad_enabled() and source_points.requires_grad:
@@ -303,6 +332,7 @@ def query_knn(
     query_offsets: torch.Tensor | None = None,
     source_points: torch.Tensor | None = None,
     sort_queries: bool = True,
+    out=None,
 ):
     """Query exact k-NN. Dispatches on handle type.
 
@@ -312,14 +342,21 @@ def query_knn(
 
     Returns ``(indices, squared_distances)`` or, when ``source_points`` is provided,
     ``(indices, squared_distances, neighbor_positions)``.
+
+    ``out=(indices, squared_distances)`` (an addition to the reference's
+    signature) writes the result into caller-owned tensors of the result shape,
+    on the BVH's device or in pinned host memory, and returns them. Pinned host
+    tensors are filled by the traversal itself across PCIe, so no device copy of
+    the result is made; read them after the current stream has passed the call
+    (``torch.cuda.current_stream().synchronize()`` or an event).
     """
     if isinstance(bvh, RaggedBVHHandle):
         _reject_unless(query_offsets is not None, "query_knn: query_offsets is required when querying a ragged BVH")
-        return _query_knn_ragged(bvh, query_points, query_offsets, k, source_points=source_points)
+        return _query_knn_ragged(bvh, query_points, query_offsets, k, source_points=source_points, out=out)
     if query_offsets is not None:
         raise TypeError("query_knn: query_offsets requires a RaggedBVHHandle")
     run = _query_knn_batched if isinstance(bvh, BatchedBVHHandle) else _query_knn_single
-    return run(bvh, query_points, k, source_points=source_points, sort_queries=sort_queries)
+    return run(bvh, query_points, k, source_points=source_points, sort_queries=sort_queries, out=out)
 
 
 # ---------------------------------------------------------------------------

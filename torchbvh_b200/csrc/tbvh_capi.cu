@@ -39,6 +39,26 @@ int set_device(int device, const char* op) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Whether the traversal on the current device may store to `p`: memory of that
+// device, managed memory, or page-locked host memory mapped at the same address
+// (unified addressing), which the kernel then fills across PCIe. Pageable host
+// memory and other devices' memory are refused here, before a launch could fault.
+bool kernel_writable(const void* p) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  switch (at.type) {
+    case cudaMemoryTypeDevice: return at.device == dev;
+    case cudaMemoryTypeManaged: return true;
+    case cudaMemoryTypeHost: return at.devicePointer == p;
+    default: return false;
+  }
+}
+
 // Cloud description shared by build and query.
 struct Clouds {
   int64_t num = 0;
@@ -387,6 +407,9 @@ int tbvh_query_knn_gather(int device, const float* node_aabbs, const int64_t* so
                 workspace_bytes, need);
   rc = set_device(device, op);
   if (rc) return rc;
+  if (!kernel_writable(out_indices) || !kernel_writable(out_distances) ||
+      (out_positions && !kernel_writable(out_positions)))
+    return fail(TBVH_ERR_BAD_ARG, "%s: outputs must be memory of this device or page-locked host memory", op);
   tbvh::KnnLaunch q{};
   q.node_aabbs = node_aabbs;
   q.sorted_indices = sorted_indices;
