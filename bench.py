@@ -22,8 +22,7 @@ queries, k = 32). Metric: k-NN queries/sec (build + query).
   scaling).
 * ``e2e``: the same public API with the inputs in pinned host memory: per step
   H2D copy of points and queries, build, query with ``out=`` pinned host
-  tensors (the traversal stores the indices and distances across PCIe as it
-  runs), all inside the events.
+  tensors (D2H copy of indices and distances), all inside the events.
 * ``roofline``: the traversal kernel (dominant), algorithmic query bytes per
   launch over its event-timed duration, against MEASURED_PEAKS.json hbm_gbs.
 * ``cpu_baseline``: the CPU port of the reference algorithm (oracle/, C,
@@ -356,8 +355,8 @@ def run_b200(args, world, rank, local):
             q = hq.to(device, non_blocking=True)
             o = ho.to(device, non_blocking=True) if ho is not None else None
             qo = hqo.to(device, non_blocking=True) if hqo is not None else None
-            # The traversal stores every result row straight into the pinned
-            # host tensors (out=), across PCIe while it runs.
+            # out= pinned host tensors: the result is copied into them on the
+            # current stream (one bulk D2H copy per tensor).
             step(p, q, o, qo, (out_idx, out_dist))
 
         for _ in range(2):

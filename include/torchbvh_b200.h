@@ -145,7 +145,10 @@ int tbvh_sort_queries_noalloc(int device, const float* queries, int64_t num_clou
  * page-locked host memory (cudaHostAlloc / cudaHostRegister, mapped at the
  * same address): the kernel then stores the finished rows across PCIe as it
  * goes, and they are readable on the host once the stream has passed the
- * call. Any other output pointer (pageable host memory, another device's
+ * call. Rows land at scattered query rows, which PCIe serves slowly (16.5 GB/s
+ * measured for 6.4 GB of rows on B200, against 52 GB/s for one bulk copy of a
+ * device result), so for large outputs a device result plus one copy is
+ * faster. Any other output pointer (pageable host memory, another device's
  * memory) returns TBVH_ERR_BAD_ARG before a launch.
  */
 size_t tbvh_query_knn_workspace_size(int64_t num_clouds, int64_t points_per_cloud);

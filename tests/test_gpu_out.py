@@ -1,7 +1,8 @@
 """``knn(..., out=(indices, squared_distances))``: results written into
-caller-owned tensors, on the device or in pinned host memory (the traversal
-then stores every row across PCIe itself). Rows must equal the allocating call
-bit for bit on every layout (single, batched, ragged) and both top-k forms."""
+caller-owned tensors, on the device (by the traversal) or in pinned host memory
+(by a copy). Rows must equal the allocating call bit for bit on every layout
+(single, batched, ragged) and both top-k forms. The C ABI's direct stores into
+page-locked host memory are checked through the raw entry point."""
 from __future__ import annotations
 
 import numpy as np
@@ -101,3 +102,25 @@ def test_c_abi_refuses_pageable_output_before_launch():
         assert b"page-locked" in lib.tbvh_last_error()
         assert lib.tbvh_kernel_launch_count() == launches
     assert not host_idx.any()
+
+
+@pytest.mark.parametrize("k", [8, 32])
+def test_c_abi_stores_rows_into_page_locked_host_memory(k):
+    """Outputs in page-locked host memory (mapped at the same address) are
+    written by the traversal itself, row for row equal to a device result."""
+    points = _rand(11, (30_000, 3)).cuda()
+    queries = _rand(12, (5_000, 3)).cuda()
+    with torchbvh.BVH(points) as bvh:
+        want_i, want_d = bvh.knn(queries, k)
+        h = bvh._handle
+        order = _native._C.morton_sort_queries_narrow(queries.unsqueeze(0), h["scene_min"].unsqueeze(0),
+                                                      h["scene_max"].unsqueeze(0)).contiguous()
+        host_i, host_d = _outs((5_000, k), "pinned")
+        lib = _native.load_library()
+        rc = lib.tbvh_query_knn(0, h["node_aabbs"].data_ptr(), h["sorted_indices"].data_ptr(), 1, 30_000, None, None,
+                                queries.data_ptr(), 5_000, None, 5_000, order.data_ptr(), 3, k,
+                                host_i.data_ptr(), host_d.data_ptr(), None, 0, _native._stream(queries.device))
+        assert rc == 0
+        torch.cuda.current_stream().synchronize()
+    assert torch.equal(host_i, want_i.cpu()) and torch.equal(host_d, want_d.cpu())
+    assert torchbvh.device_status() == 0

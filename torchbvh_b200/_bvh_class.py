@@ -47,7 +47,8 @@ class BVH:
         For ragged BVHs ``query_offsets`` is required. For single/batched BVHs
         ``sort_queries`` controls Morton-sorted traversal (default True).
         ``out=(indices, squared_distances)``: caller-owned result tensors on the
-        BVH's device or in pinned host memory (filled by the traversal itself).
+        BVH's device (written by the traversal) or in pinned host memory (an
+        asynchronous copy on the current stream).
         """
         return query_knn(self._handle, query_points, k, query_offsets=query_offsets, source_points=source_points,
                          sort_queries=sort_queries, out=out)
