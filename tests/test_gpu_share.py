@@ -170,3 +170,20 @@ def test_int32_destinations_widen_to_the_int64_result(k):
     assert torch.equal(wide, want_i) and torch.equal(dd[0], want_d) and torch.equal(dd[1], want_d)
     assert torch.equal(wire[0].long(), want_i)
     assert torchbvh.device_status() == 0
+
+
+def test_two_and_three_dimensional_shares_in_one_process():
+    """The share-cells kernel opts in to 128 KB of shared memory separately for
+    its 2-D and 3-D forms: selecting shares of a 3-D cloud and then of a 2-D one
+    (and back) in one process must work for both."""
+    from torchbvh_b200 import distributed as tdist
+
+    for dim in (3, 2, 3):
+        g = torch.Generator().manual_seed(80 + dim)
+        points = torch.rand((20_000, dim), generator=g).cuda()
+        queries = torch.rand((10_003, dim), generator=g).cuda()
+        with torchbvh.BVH(points) as bvh:
+            shares = [tdist._owned_queries_cuda(bvh._handle, queries, r, 3, "morton") for r in range(3)]
+        torch.cuda.synchronize()
+        assert torch.equal(torch.sort(torch.cat(shares).cpu()).values, torch.arange(10_003))
+    assert torchbvh.device_status() == 0

@@ -171,6 +171,46 @@ __device__ __forceinline__ void flush_box(uint32_t* enc, int cloud, const float*
   }
 }
 
+// Points 4·qd .. 4·qd + 3 that lie below `end`. A quad of 3-D points is 48
+// contiguous bytes (three float4), of 2-D points 32 (two float4): when the
+// array is 16-byte aligned and the quad whole, it arrives in 128-bit loads;
+// otherwise point by point (points at or past `end` read as 0 and are unused).
+template <int D>
+__device__ __forceinline__ void load_quad(const float* __restrict__ pts, int64_t qd, int64_t end, bool vec,
+                                          float (&p)[4][D]) {
+  const int64_t i0 = qd * 4;
+  if (vec && i0 + 4 <= end) {
+    const float4* v = reinterpret_cast<const float4*>(pts + i0 * D);
+    float f[4 * D];
+#pragma unroll
+    for (int j = 0; j < D; ++j) {
+      const float4 x = __ldg(v + j);
+      f[4 * j] = x.x;
+      f[4 * j + 1] = x.y;
+      f[4 * j + 2] = x.z;
+      f[4 * j + 3] = x.w;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int a = 0; a < D; ++a) p[u][a] = f[u * D + a];
+  } else {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int a = 0; a < D; ++a) p[u][a] = i0 + u < end ? __ldg(pts + (i0 + u) * D + a) : 0.0f;
+  }
+}
+
+// Quads of points each k_keys thread has in flight (loaded before any is used).
+#ifndef TBVH_KEYS_QUADS
+#define TBVH_KEYS_QUADS 2
+#endif
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) k_bounds(const float* __restrict__ pts, CloudMap cm, int64_t n,
                                                 int64_t chunk, uint32_t* __restrict__ enc) {
@@ -183,22 +223,31 @@ __global__ void __launch_bounds__(256) k_bounds(const float* __restrict__ pts, C
   float lo[D], hi[D];
 #pragma unroll
   for (int a = 0; a < D; ++a) { lo[a] = 1.0e30f; hi[a] = -1.0e30f; }
-  for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
-    if (i >= cur_end) {
-      const int c = cm.find(i);
-      if (cur >= 0 && c != cur) {
-        flush_box<D>(enc, cur, lo, hi);
+  // The chunk starts on a multiple of 256 points, so its quads are whole
+  // quads of the array; each thread takes every 256th quad.
+  const bool vec = aligned16(pts);
+  for (int64_t qd = begin / 4 + threadIdx.x; qd * 4 < end; qd += blockDim.x) {
+    float p[4][D];
+    load_quad<D>(pts, qd, end, vec, p);
 #pragma unroll
-        for (int a = 0; a < D; ++a) { lo[a] = 1.0e30f; hi[a] = -1.0e30f; }
+    for (int u = 0; u < 4; ++u) {
+      const int64_t i = qd * 4 + u;
+      if (i >= end) break;
+      if (i >= cur_end) {
+        const int c = cm.find(i);
+        if (cur >= 0 && c != cur) {
+          flush_box<D>(enc, cur, lo, hi);
+#pragma unroll
+          for (int a = 0; a < D; ++a) { lo[a] = 1.0e30f; hi[a] = -1.0e30f; }
+        }
+        cur = c;
+        cur_end = cm.start(c) + cm.size(c);
       }
-      cur = c;
-      cur_end = cm.start(c) + cm.size(c);
-    }
 #pragma unroll
-    for (int a = 0; a < D; ++a) {
-      const float v = pts[i * D + a];
-      lo[a] = fminf(lo[a], v);
-      hi[a] = fmaxf(hi[a], v);
+      for (int a = 0; a < D; ++a) {
+        lo[a] = fminf(lo[a], p[u][a]);
+        hi[a] = fmaxf(hi[a], p[u][a]);
+      }
     }
   }
   const unsigned lane = lane_id();
@@ -251,8 +300,9 @@ __global__ void __launch_bounds__(256) k_bounds(const float* __restrict__ pts, C
 
 // ---------------------------------------------------------------------------
 // Morton keys + digit histograms for every sort pass (one read of the
-// coordinates). Histograms are aggregated per warp with match_any, per block
-// in shared memory, then added to the global per-pass histograms.
+// coordinates). Each lane counts its digits into the block's shared
+// histograms (a digit the whole warp shares is counted once by one lane),
+// which are then added to the global per-pass histograms.
 // ---------------------------------------------------------------------------
 template <int D, bool kEncodedBounds>
 __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, CloudMap cm, int64_t n,
@@ -273,60 +323,74 @@ __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, Clo
   }
   __syncthreads();
   const unsigned lane = lane_id();
-  const int64_t rounds = (n + int64_t(gridDim.x) * blockDim.x - 1) / (int64_t(gridDim.x) * blockDim.x);
+  // Each thread takes whole quads of 4 consecutive points (128-bit loads of
+  // the coordinates, one 128-bit store of the 4 keys), two quads in flight.
+  const int64_t nq = (n + 3) / 4;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t rounds = (nq + stride - 1) / stride;
+  const bool vec = aligned16(pts);
+  const bool vec_keys = aligned16(keys);
   int cur = -1;
   int64_t cur_end = -1;
   float lo[D], hi[D];
-  // Rounds go in groups of four whose points are all loaded before any is
-  // used, so each thread has four loads in flight instead of one.
-  constexpr int kGroup = 4;
+  constexpr int kGroup = TBVH_KEYS_QUADS;
   for (int64_t r0 = 0; r0 < rounds; r0 += kGroup) {
-    float pg[kGroup][D];
+    float pg[kGroup][4][D];
 #pragma unroll
     for (int u = 0; u < kGroup; ++u) {
-      const int64_t i = ((r0 + u) * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
-      if (r0 + u < rounds && i < n) {
-#pragma unroll
-        for (int a = 0; a < D; ++a) pg[u][a] = __ldg(pts + i * D + a);
-      }
+      const int64_t qd = (r0 + u) * stride + int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+      if (r0 + u < rounds && qd < nq) load_quad<D>(pts, qd, n, vec, pg[u]);
     }
 #pragma unroll
     for (int u = 0; u < kGroup; ++u) {
-      const int64_t r = r0 + u;
-      if (r >= rounds) break;  // uniform across the grid
-      const int64_t i = (r * gridDim.x + blockIdx.x) * int64_t(blockDim.x) + threadIdx.x;
-      const bool valid = i < n;
-      uint32_t code = 0;
-      int c = 0;
-      if (valid) {
-        if (i >= cur_end || cur < 0) {
-          cur = cm.find(i);
-          cur_end = cm.start(cur) + cm.size(cur);
+      if (r0 + u >= rounds) break;  // uniform across the grid
+      const int64_t qd = (r0 + u) * stride + int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+      uint32_t code4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int a = 0; a < D; ++a) {
-            if (kEncodedBounds) {
-              lo[a] = ordered_to_float(enc[cur * 2 * D + a]);
-              hi[a] = ordered_to_float(enc[cur * 2 * D + D + a]);
-            } else {
-              lo[a] = smin[cur * D + a];
-              hi[a] = smax[cur * D + a];
+      for (int v = 0; v < 4; ++v) {
+        const int64_t i = qd * 4 + v;
+        const bool valid = qd < nq && i < n;
+        uint32_t code = 0;
+        int c = 0;
+        if (valid) {
+          if (i >= cur_end || cur < 0) {
+            cur = cm.find(i);
+            cur_end = cm.start(cur) + cm.size(cur);
+#pragma unroll
+            for (int a = 0; a < D; ++a) {
+              if (kEncodedBounds) {
+                lo[a] = ordered_to_float(enc[cur * 2 * D + a]);
+                hi[a] = ordered_to_float(enc[cur * 2 * D + D + a]);
+              } else {
+                lo[a] = smin[cur * D + a];
+                hi[a] = smax[cur * D + a];
+              }
             }
           }
+          c = cur;
+          code = morton_code<D>(pg[u][v], lo, hi);
+          code4[v] = code;
         }
-        c = cur;
-        code = morton_code<D>(pg[u], lo, hi);
-        keys[i] = code;
+        // Digits of Morton codes in input order are mostly distinct within a warp,
+        // so each lane adds its own count; only a digit the whole warp shares (the
+        // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
+        for (int ps = 0; ps < passes; ++ps) {
+          const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
+          const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
+          if (__all_sync(kFullMask, d == d0)) {
+            if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);
+          } else if (d < 0x100u) {
+            atomicAdd(&s_hist[ps][d], 1u);
+          }
+        }
       }
-      // Digits of Morton codes in input order are mostly distinct within a warp,
-      // so each lane adds its own count; only a digit the whole warp shares (the
-      // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
-      for (int ps = 0; ps < passes; ++ps) {
-        const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
-        const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
-        if (__all_sync(kFullMask, d == d0)) {
-          if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);
-        } else if (d < 0x100u) {
-          atomicAdd(&s_hist[ps][d], 1u);
+      if (qd < nq) {
+        if (vec_keys && qd * 4 + 4 <= n) {
+          reinterpret_cast<uint4*>(keys)[qd] = make_uint4(code4[0], code4[1], code4[2], code4[3]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            if (qd * 4 + v < n) keys[qd * 4 + v] = code4[v];
         }
       }
     }
@@ -882,13 +946,27 @@ __global__ void __launch_bounds__(kShareThreads) k_share_cells(const float* __re
   for (int a = 0; a < D; ++a) { lo[a] = smin[a]; hi[a] = smax[a]; }
   __syncthreads();
   constexpr int shift = morton_bits<D>() - kShareBits;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < m; i += int64_t(gridDim.x) * blockDim.x) {
-    float p[D];
+  // Whole quads of 4 consecutive queries per thread (128-bit loads and stores).
+  const bool vec = aligned16(q), vec_codes = aligned16(codes);
+  const int64_t nq = (m + 3) / 4;
+  for (int64_t qd = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; qd < nq; qd += int64_t(gridDim.x) * blockDim.x) {
+    float p[4][D];
+    load_quad<D>(q, qd, m, vec, p);
+    uint32_t code4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int a = 0; a < D; ++a) p[a] = q[i * D + a];
-    const uint32_t code = morton_code<D>(p, lo, hi);
-    codes[i] = code;
-    atomicAdd(&s_cells[code >> shift], 1u);
+    for (int v = 0; v < 4; ++v) {
+      if (qd * 4 + v < m) {
+        code4[v] = morton_code<D>(p[v], lo, hi);
+        atomicAdd(&s_cells[code4[v] >> shift], 1u);
+      }
+    }
+    if (vec_codes && qd * 4 + 4 <= m) {
+      reinterpret_cast<uint4*>(codes)[qd] = make_uint4(code4[0], code4[1], code4[2], code4[3]);
+    } else {
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        if (qd * 4 + v < m) codes[qd * 4 + v] = code4[v];
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < kShareCells; i += blockDim.x) {
@@ -1178,7 +1256,7 @@ cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream) {
   else k_bounds<2><<<bgrid, 256, 0, stream>>>(b.points, b.clouds, n, chunk, b.bounds_enc);
   count_launches(1);
   // 3. keys + histograms
-  const int kgrid = grid_for(n, 256, 148 * 8);
+  const int kgrid = grid_for((n + 3) / 4, 256, 148 * 8);  // one thread per quad of points
   if (D == 3)
     k_keys<3, true><<<kgrid, 256, 0, stream>>>(b.points, b.clouds, n, b.bounds_enc, nullptr, nullptr,
                                                 b.ss.keys[0], b.ss.hist, p.code_bits, p.passes,
@@ -1228,7 +1306,7 @@ cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream) {
   ia.clouds = q.clouds;
   k_init<<<grid_for(p.tiles * kRadix * 2, 256 * 4, 1184), 256, 0, stream>>>(ia);
   count_launches(1);
-  const int kgrid = grid_for(n, 256, 148 * 8);
+  const int kgrid = grid_for((n + 3) / 4, 256, 148 * 8);  // one thread per quad of points
   if (D == 3)
     k_keys<3, false><<<kgrid, 256, 0, stream>>>(q.queries, q.clouds, n, nullptr, q.scene_min, q.scene_max,
                                                  q.ss.keys[0], q.ss.hist, p.code_bits, p.passes, nullptr, nullptr);
@@ -1285,16 +1363,17 @@ cudaError_t launch_share_queries(const ShareLaunch& q, int64_t* count_out, cudaS
   k_init<<<grid_for(full.tiles * kRadix * 2, 256 * 4, 1184), 256, 0, stream>>>(ia);
   count_launches(1);
   const size_t cells_smem = size_t(kShareCells) * 4;
-  static bool attr_set[64] = {};
+  // The shared-memory opt-in is per kernel (2-D and 3-D) and per device.
+  static bool attr_set[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  if (dev < 0 || dev >= 64 || !attr_set[D - 2][dev]) {
     cudaError_t e = D == 3 ? cudaFuncSetAttribute(k_share_cells<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   int(cells_smem))
                            : cudaFuncSetAttribute(k_share_cells<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   int(cells_smem));
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[D - 2][dev] = true;
   }
   // Blocks of 1,024 threads with a 128 KB cell histogram each: about 128 K
   // queries per block keeps the per-block flush of the table cheap.

@@ -107,6 +107,15 @@ static_assert(TBVH_KNN_UNION_CAP >= 32, "the union holds at least k <= 32 leaves
 #ifndef TBVH_KNN_PROFILE
 #define TBVH_KNN_PROFILE 0
 #endif
+// Levels of the tree, from the root, that a warp copies into shared memory
+// (coalesced, once per cloud it serves) and reads node boxes of from there
+// instead of through L1. 0: off (every box comes through L1).
+#ifndef TBVH_KNN_TOP_LEVELS
+#define TBVH_KNN_TOP_LEVELS 0
+#endif
+constexpr int kTopLevels = TBVH_KNN_TOP_LEVELS;
+static_assert(kTopLevels >= 0 && kTopLevels <= 10, "staged top levels: 0..10");
+constexpr int kTopRows = kTopLevels > 0 ? (1 << kTopLevels) - 1 : 1;
 #if TBVH_KNN_PROFILE
 __device__ unsigned long long g_knn_profile[16];
 #define KNN_PF_LAP(slot)                  \
@@ -155,6 +164,7 @@ struct KnnSmem {
   uint32_t stack_node[kKnnWarps][kStackDepth];
   float stack_dist[kStackBounds ? kKnnWarps : 1][kStackBounds ? kStackDepth : 1][32];
   u64 heap[heap_topk<K>() ? kKnnWarps : 1][heap_topk<K>() ? K : 1][32];  // [warp][slot][lane]
+  float top[kTopLevels > 0 ? kKnnWarps : 1][kTopRows * 6];                 // staged top-level node rows
 };
 
 // A top-k slot is one 64-bit key: distance bits above, source index below.
@@ -468,6 +478,28 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
   float root_lo[D], root_hi[D];
   load_box<D>(rows, 0, root_lo, root_hi);
 
+  // Top levels staged in shared memory (rows [0, top_rows): whole levels).
+  int64_t top_rows = 0;
+  if constexpr (kTopLevels > 0) {
+    top_rows = kTopLevels <= L ? __shfl_sync(kFullMask, my_rowoff, kTopLevels) : leaf_row0 + n;
+    if (top_rows > kTopRows) top_rows = kTopRows;  // whole levels never exceed it; kept for safety
+    for (int i = int(lane); i < int(top_rows) * 2 * D; i += 32) s.top[warp][i] = __ldg(rows + i);
+    __syncwarp();
+  }
+  // Box of node row `row` (warp-uniform).
+  auto node_box = [&](int64_t row, float* lo, float* hi) {
+    if (kTopLevels > 0 && row < top_rows) {
+      const float* r = &s.top[kTopLevels > 0 ? warp : 0][int(row) * 2 * D];
+#pragma unroll
+      for (int c = 0; c < D; ++c) {
+        lo[c] = r[c];
+        hi[c] = r[D + c];
+      }
+    } else {
+      load_box<D>(rows, row, lo, hi);
+    }
+  };
+
   // Query.
   float q[D];
   int64_t gq = 0;
@@ -695,7 +727,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
           dg[g] = INFINITY;
           if (g < gleft) {
             float lo[D], hi[D];
-            load_box<D>(rows, grow + g, lo, hi);
+            node_box(grow + g, lo, hi);
             dg[g] = box_dist2<D>(q, lo, hi);
           }
         }
@@ -760,11 +792,11 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
         const int64_t crow = __shfl_sync(kFullMask, my_rowoff, cl) + c0;
         const bool right_real = c0 + 1 < ccnt;
         float lo[D], hi[D];
-        load_box<D>(rows, crow, lo, hi);
+        node_box(crow, lo, hi);
         const float d0 = box_dist2<D>(q, lo, hi);
         float d1 = INFINITY;
         if (right_real) {
-          load_box<D>(rows, crow + 1, lo, hi);
+          node_box(crow + 1, lo, hi);
           d1 = box_dist2<D>(q, lo, hi);
         }
         const bool n0 = d0 <= kth;
@@ -812,7 +844,7 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
           d = s.stack_dist[warp][sp][lane];
         } else {
           float lo[D], hi[D];
-          load_box<D>(rows, __shfl_sync(kFullMask, my_rowoff, el) + ej, lo, hi);
+          node_box(__shfl_sync(kFullMask, my_rowoff, el) + ej, lo, hi);
           d = box_dist2<D>(q, lo, hi);
         }
         if (__any_sync(kFullMask, d <= kth)) {
