@@ -18,8 +18,10 @@ queries, k = 32). Metric: k-NN queries/sec (build + query).
   each row into all ranks' buffers over NVLink), i.e. results all-gathered;
   ``results_in_place`` times the same step with the rows left on the rank
   that computed them, ``nccl_all_gather`` with an NCCL all-gather after the
-  traversal instead. The other workloads on N GPUs run N replicas (weak
-  scaling).
+  traversal instead. c2 / c3 / c5 on N GPUs are sharded by cloud (strong
+  scaling: each rank builds and queries its clouds, results all-gathered by
+  NCCL); ``--replicas`` runs N independent replicas instead (weak scaling);
+  c1 always runs replicas.
 * ``e2e``: the same public API with the inputs in pinned host memory: per step
   H2D copy of points and queries, build, query with ``out=`` pinned host
   tensors (D2H copy of indices and distances), all inside the events.
@@ -65,6 +67,9 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference_cuda"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="c2 / c3 / c5 on N > 1 GPUs: N independent replicas of the whole workload "
+                         "(weak scaling) instead of the clouds sharded over the ranks")
     ap.add_argument("--c4-points", type=int, default=16_777_216,
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
     ap.add_argument("--c4-index-bits", type=int, default=32, choices=[32, 64],
@@ -438,6 +443,86 @@ def run_b200(args, world, rank, local):
         "gpu": torch.cuda.get_device_name(device),
     }
     return result
+
+
+def run_b200_clouds_sharded(args, world, rank, local):
+    """c2 / c3 / c5 on N > 1 GPUs, sharded by cloud (strong scaling).
+
+    Every rank holds the whole batch; one step is
+    ``distributed.knn_sharded_batched`` (fixed-size clouds split into contiguous
+    ranges) or ``knn_sharded_ragged`` (ragged clouds by a longest-first
+    partition): each rank builds and queries its clouds, then the results are
+    all-gathered (NCCL) into the original order on every rank.
+    """
+    from torchbvh_b200 import _native
+    from torchbvh_b200 import distributed as tdist
+    import torchbvh_b200 as torchbvh
+
+    device = torch.device("cuda", local)
+    w = load_workload(args.workload, args)
+    k = w.k
+    points = w.points.to(device)
+    queries = w.queries.to(device)
+    if w.batch_offsets is not None:
+        bo = [int(v) for v in w.batch_offsets.tolist()]
+        qo = [int(v) for v in w.query_offsets.tolist()]
+
+        def step():
+            return tdist.knn_sharded_ragged(points, bo, queries, qo, k)
+        form = "knn_sharded_ragged: clouds by a longest-first partition of their sizes"
+    else:
+        def step():
+            return tdist.knn_sharded_batched(points, queries, k)
+        form = "knn_sharded_batched: contiguous cloud ranges"
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    out = None
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    launches0 = _native.load_library().tbvh_kernel_launch_count()
+    ev = []
+    sampler = ClockSampler(local)
+    with sampler:
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            out = step()
+            b.record(stream)
+            ev.append((a, b))
+        torch.cuda.synchronize(device)
+    del out
+    launches = _native.load_library().tbvh_kernel_launch_count() - launches0
+    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), world)
+    cfg = workload_config(w, world)
+    cfg["parallelism"] = (f"{form} over {world} GPUs, every result row all-gathered (NCCL) into the "
+                          f"original order on every rank")
+    return {
+        "metric": METRIC,
+        "value": w.num_queries * args.steps / (total_ms / 1e3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded CPU generator, torchbvh_b200.workloads)",
+        "config": cfg,
+        "roofline": None,
+        "cpu_baseline": None,
+        "e2e": None,
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps,
+        "device_status": torchbvh.device_status(device),
+        "clocks": sampler.summary(),
+        "gpu": torch.cuda.get_device_name(device),
+    }
 
 
 def run_b200_single_cloud_sharded(args, world, rank, local):
@@ -920,6 +1005,8 @@ def main():
             result = run_reference_cuda(args, world, rank, local)
         elif args.workload == "c4" and world > 1:
             result = run_b200_single_cloud_sharded(args, world, rank, local)
+        elif args.workload in ("c2", "c3", "c5") and world > 1 and not args.replicas:
+            result = run_b200_clouds_sharded(args, world, rank, local)
         else:
             result = run_b200(args, world, rank, local)
         if rank == 0 and result is not None:

@@ -203,8 +203,10 @@ __device__ __forceinline__ void load_quad(const float* __restrict__ pts, int64_t
 }
 
 // Quads of points each k_keys thread has in flight (loaded before any is used).
+// Measured on B200 (build ms, c4 / c2 / c5): 1 quad 1.583 / 0.198 / 1.166,
+// 2 quads 1.592 / 0.198 / 1.190 (64 registers), scalar loads 1.598 / 0.206 / 1.219.
 #ifndef TBVH_KEYS_QUADS
-#define TBVH_KEYS_QUADS 2
+#define TBVH_KEYS_QUADS 1
 #endif
 
 __device__ __forceinline__ bool aligned16(const void* p) {
@@ -372,10 +374,15 @@ __global__ void __launch_bounds__(256) k_keys(const float* __restrict__ pts, Clo
           code4[v] = code;
         }
         // Digits of Morton codes in input order are mostly distinct within a warp,
-        // so each lane adds its own count; only a digit the whole warp shares (the
-        // cloud-id digits) is added once, to avoid a 32-way conflict on one bin.
+        // so each lane adds its own count. A digit that holds cloud-id bits is
+        // often the same for the whole warp: it is added once, by one lane, to
+        // avoid a 32-way conflict on one bin (passes of code bits only skip the test).
         for (int ps = 0; ps < passes; ++ps) {
           const uint32_t d = valid ? composite_digit(code, uint32_t(c), code_bits, 8 * ps) : 0x100u;
+          if (8 * ps + 8 <= code_bits || cm.num_clouds == 1) {  // uniform across the grid
+            if (d < 0x100u) atomicAdd(&s_hist[ps][d], 1u);
+            continue;
+          }
           const uint32_t d0 = __shfl_sync(kFullMask, d, 0);
           if (__all_sync(kFullMask, d == d0)) {
             if (lane == 0 && d0 < 0x100u) atomicAdd(&s_hist[ps][d0], 32u);

@@ -91,6 +91,8 @@ _phase_hooks: list = []
 def _phase(name: str, device) -> None:
     for hook in _phase_hooks:
         hook(name, device)
+
+
 _RUNS_PER_RANK = 32  # ownership runs per rank of the interleaved split
 
 
@@ -404,12 +406,13 @@ def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: 
     qcount = [sum(query_offsets[c + 1] - query_offsets[c] for c in parts[r]) for r in range(world)]
     all_idx = _all_gather_rows(idx, qcount, group)
     all_dist = _all_gather_rows(dist_sq, qcount, group)
-    # Back to the original packed order.
-    order = []
-    for r in range(world):
-        for c in parts[r]:
-            order.extend(range(query_offsets[c], query_offsets[c + 1]))
-    inverse = torch.empty(len(order), dtype=torch.int64)
-    inverse[torch.tensor(order, dtype=torch.int64)] = torch.arange(len(order), dtype=torch.int64)
-    inverse = inverse.to(all_idx.device)
-    return all_idx.index_select(0, inverse), all_dist.index_select(0, inverse)
+    # Back to the original packed order: gathered row p (clouds rank by rank, each
+    # rank's clouds ascending) is packed query row owner[p], computed on the device.
+    clouds = [c for r in range(world) for c in parts[r]]
+    lens = torch.tensor([query_offsets[c + 1] - query_offsets[c] for c in clouds], dtype=torch.int64)
+    gathered_start = torch.cumsum(lens, 0) - lens
+    shift = torch.tensor([query_offsets[c] for c in clouds], dtype=torch.int64) - gathered_start
+    total = int(lens.sum())
+    owner = torch.repeat_interleave(shift.to(dev), lens.to(dev), output_size=total) + \
+        torch.arange(total, dtype=torch.int64, device=dev)
+    return _to_query_order(all_idx, owner), _to_query_order(all_dist, owner)
