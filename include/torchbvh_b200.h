@@ -200,6 +200,17 @@ int tbvh_peer_free(int device, void* ptr);
 int tbvh_peer_open(int device, const void* handle, void** out_ptr);
 int tbvh_peer_close(int device, void* ptr);
 
+/* Scene box of one cloud of num_points points: scene_min / scene_max (dim
+ * floats each, device). The scene-AABB reduction of the build alone
+ * (torchbvh/csrc/bvh_build.cu:453-494, the reduction tbvh_build runs first),
+ * bit-identical to the scene_min / scene_max tbvh_build returns for the same
+ * points. Lets a caller start work that needs only the box (the Morton share
+ * of a sharded cloud's queries) on another stream while the build runs.
+ * Workspace: tbvh_scene_bounds_workspace_size() bytes of device scratch. */
+size_t tbvh_scene_bounds_workspace_size(void);
+int tbvh_scene_bounds(int device, const float* points, int64_t num_points, int dim, float* scene_min,
+                      float* scene_max, void* workspace, size_t workspace_bytes, void* stream);
+
 /* This rank's share of the num_queries queries of one cloud, in Morton order
  * (codes against scene_min/scene_max, the BVH's scene box). No counterpart in
  * the reference. The code range is cut at cells of its top 15 bits; walking

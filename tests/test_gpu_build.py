@@ -130,3 +130,43 @@ def test_build_rejects_unsupported_inputs():
         torchbvh.build_bvh(torch.zeros((4, 4), device="cuda"))
     with pytest.raises(ValueError, match="float32"):
         torchbvh.build_bvh(torch.zeros((4, 2), device="cuda", dtype=torch.float64))
+
+
+@pytest.mark.parametrize("d", [2, 3])
+@pytest.mark.parametrize("n", [1, 5, 4097, 300_001])
+def test_unaligned_points_build_the_same_tree(d, n):
+    """The bounds and key kernels read points in 128-bit quads when the array
+    is 16-byte aligned and point by point otherwise: a view that starts one
+    point into its storage (4·D bytes, never 16-byte aligned) must give the
+    same tree, box and query order as an aligned copy."""
+    g = torch.Generator().manual_seed(500 + d + n)
+    base = torch.rand((n + 1, d), generator=g).cuda()
+    view = base[1:]
+    assert view.data_ptr() % 16 != 0 and view.is_contiguous()
+    copy = view.clone()
+    assert copy.data_ptr() % 16 == 0
+    qbase = torch.rand((n + 1, d), generator=g).cuda()
+    a = torchbvh.build_bvh(view)
+    b = torchbvh.build_bvh(copy)
+    for key in ("node_aabbs", "sorted_indices", "scene_min", "scene_max"):
+        assert torch.equal(a[key], b[key]), key
+    if n >= 4:
+        ia, da = torchbvh.query_knn(a, qbase[1:], 4)
+        ib, db = torchbvh.query_knn(b, qbase[1:].clone(), 4)
+        assert torch.equal(ia, ib) and torch.equal(da, db)
+    assert torchbvh.device_status() == 0
+
+
+@pytest.mark.parametrize("d", [2, 3])
+@pytest.mark.parametrize("n", [1, 7, 100_003])
+def test_scene_bounds_alone_equal_the_builds(d, n):
+    """tbvh_scene_bounds gives the build's scene box bit for bit (aligned and
+    unaligned point arrays)."""
+    from torchbvh_b200 import _native
+
+    g = torch.Generator().manual_seed(600 + d + n)
+    base = (torch.randn((n + 1, d), generator=g) * 50.0 + 3.0).cuda()
+    for pts in (base[1:], base[1:].clone()):
+        lo, hi = _native.scene_bounds(pts)
+        h = torchbvh.build_bvh(pts)
+        assert torch.equal(lo, h["scene_min"]) and torch.equal(hi, h["scene_max"])

@@ -187,3 +187,21 @@ def test_two_and_three_dimensional_shares_in_one_process():
         torch.cuda.synchronize()
         assert torch.equal(torch.sort(torch.cat(shares).cpu()).values, torch.arange(10_003))
     assert torchbvh.device_status() == 0
+
+
+def test_unaligned_queries_give_the_same_shares():
+    """The share-cells kernel reads queries in 128-bit quads only from a 16-byte
+    aligned array: a view one query into its storage must select the same shares."""
+    from torchbvh_b200 import distributed as tdist
+
+    g = torch.Generator().manual_seed(90)
+    points = torch.rand((30_000, 3), generator=g).cuda()
+    qbase = torch.rand((20_002, 3), generator=g).cuda()
+    view, copy = qbase[1:], qbase[1:].clone()
+    assert view.data_ptr() % 16 != 0 and copy.data_ptr() % 16 == 0
+    with torchbvh.BVH(points) as bvh:
+        for r in range(4):
+            a = tdist._owned_queries_cuda(bvh._handle, view, r, 4, "morton")
+            b = tdist._owned_queries_cuda(bvh._handle, copy, r, 4, "morton")
+            assert torch.equal(a, b)
+    assert torchbvh.device_status() == 0

@@ -65,6 +65,8 @@ _SIGNATURES = {
     "tbvh_sort_queries_workspace_size": (_size, [_i64, _i64, _i32]),
     "tbvh_sort_queries": (_i32, [_i32, _ptr, _i64, _i64, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_query_knn_workspace_size": (_size, [_i64, _i64]),
+    "tbvh_scene_bounds_workspace_size": (_size, []),
+    "tbvh_scene_bounds": (_i32, [_i32, _ptr, _i64, _i32, _ptr, _ptr, _ptr, _size, _ptr]),
     "tbvh_share_queries_workspace_size": (_size, [_i64, _i32]),
     "tbvh_share_queries": (
         _i32, [_i32, _ptr, _i64, _i32, _ptr, _ptr, _i32, _i32, _i64, _ptr, ctypes.POINTER(_i64), _ptr, _size, _ptr],
@@ -314,6 +316,21 @@ def morton_sort_queries_narrow(queries: torch.Tensor, scene_min: torch.Tensor, s
         scene_min.data_ptr(), scene_max.data_ptr(), order.data_ptr(), ws.data_ptr(), ws.numel(), _stream(device),
     ))
     return order
+
+
+def scene_bounds(points: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(scene_min, scene_max) of one (N, D) cloud on the current stream,
+    bit-identical to the build's (tbvh_scene_bounds)."""
+    if not (points.is_cuda and points.is_contiguous() and points.dtype == torch.float32 and points.dim() == 2):
+        raise RuntimeError("scene_bounds: points must be contiguous CUDA float32 (N, D)")
+    n, dim = int(points.size(0)), int(points.size(1))
+    device = points.device
+    lib = load_library()
+    box = torch.empty((2, dim), dtype=torch.float32, device=device)
+    ws = _workspace(lib.tbvh_scene_bounds_workspace_size(), device)
+    _check(lib.tbvh_scene_bounds(device.index, points.data_ptr(), n, dim, box[0].data_ptr(), box[1].data_ptr(),
+                                 ws.data_ptr(), ws.numel(), _stream(device)))
+    return box[0], box[1]
 
 
 def share_queries(queries: torch.Tensor, scene_min: torch.Tensor, scene_max: torch.Tensor, rank: int, world: int,

@@ -300,6 +300,16 @@ __global__ void __launch_bounds__(256) k_bounds(const float* __restrict__ pts, C
   }
 }
 
+// Scene box of one cloud from its order-preserving encoding (standalone bounds).
+__global__ void k_bounds_decode(const uint32_t* __restrict__ enc, int dim, float* __restrict__ smin,
+                                float* __restrict__ smax) {
+  const int a = int(threadIdx.x);
+  if (a < dim) {
+    smin[a] = ordered_to_float(enc[a]);
+    smax[a] = ordered_to_float(enc[dim + a]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Morton keys + digit histograms for every sort pass (one read of the
 // coordinates). Each lane counts its digits into the block's shared
@@ -1298,6 +1308,30 @@ cudaError_t launch_build(const BuildLaunch& b, cudaStream_t stream) {
   if (D == 3) k_tree<3><<<unsigned(b.tree_blocks), kTreeThreads, 0, stream>>>(ta);
   else k_tree<2><<<unsigned(b.tree_blocks), kTreeThreads, 0, stream>>>(ta);
   count_launches(1);
+  return cudaGetLastError();
+}
+
+// The scene box of one cloud alone: the same seeds, chunks and reductions as
+// the build's bounds step, so the result is bit-identical to the build's
+// scene_min / scene_max for the same points (min / max are exact).
+cudaError_t launch_scene_bounds(const float* points, int64_t n, int D, uint32_t* enc, float* smin, float* smax,
+                                cudaStream_t stream) {
+  CloudMap cm{};
+  cm.offsets = nullptr;
+  cm.uniform_n = n;
+  cm.num_clouds = 1;
+  InitArgs ia{};
+  ia.bounds_enc = enc;
+  ia.bounds_words = 2 * D;
+  ia.dim = D;
+  ia.clouds = cm;
+  k_init<<<1, 256, 0, stream>>>(ia);
+  const int64_t chunk = n / 1184 > 4096 ? ((n / 1184 + 255) / 256) * 256 : 4096;
+  const int bgrid = int((n + chunk - 1) / chunk);
+  if (D == 3) k_bounds<3><<<bgrid, 256, 0, stream>>>(points, cm, n, chunk, enc);
+  else k_bounds<2><<<bgrid, 256, 0, stream>>>(points, cm, n, chunk, enc);
+  k_bounds_decode<<<1, 32, 0, stream>>>(enc, D, smin, smax);
+  count_launches(3);
   return cudaGetLastError();
 }
 

@@ -321,6 +321,27 @@ int tbvh_sort_queries(int device, const float* queries, int64_t num_clouds, int6
   return TBVH_OK;
 }
 
+size_t tbvh_scene_bounds_workspace_size(void) { return 256; }
+
+int tbvh_scene_bounds(int device, const float* points, int64_t num_points, int dim, float* scene_min,
+                      float* scene_max, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "scene_bounds";
+  g_last_error.clear();
+  if (dim != 2 && dim != 3) return fail(TBVH_ERR_BAD_ARG, "%s: D must be 2 or 3", op);
+  if (num_points < 1 || num_points > INT_MAX)
+    return fail(TBVH_ERR_BAD_ARG, "%s: point count must be in [1, 2^31)", op);
+  if (!points || !scene_min || !scene_max) return fail(TBVH_ERR_BAD_ARG, "%s: NULL pointer", op);
+  if (workspace == nullptr || workspace_bytes < tbvh_scene_bounds_workspace_size())
+    return fail(TBVH_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the required %zu", op,
+                workspace_bytes, tbvh_scene_bounds_workspace_size());
+  int rc = set_device(device, op);
+  if (rc) return rc;
+  const cudaError_t e = tbvh::launch_scene_bounds(points, num_points, dim, static_cast<uint32_t*>(workspace),
+                                                  scene_min, scene_max, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, op);
+  return TBVH_OK;
+}
+
 size_t tbvh_share_queries_workspace_size(int64_t num_queries, int dim) {
   if (num_queries < 1 || num_queries > INT_MAX || (dim != 2 && dim != 3)) return 0;
   return tbvh::share_scratch_bytes(num_queries, dim);

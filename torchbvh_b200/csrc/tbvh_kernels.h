@@ -108,6 +108,10 @@ struct QuerySortLaunch {
 
 cudaError_t launch_query_sort(const QuerySortLaunch& q, cudaStream_t stream);
 
+// Scene box of one cloud (the build's bounds step alone); enc: 2·D words of scratch.
+cudaError_t launch_scene_bounds(const float* points, int64_t n, int D, uint32_t* enc, float* smin, float* smax,
+                                cudaStream_t stream);
+
 // One rank's share of the queries of one cloud, in Morton order (see
 // k_share_cells in tbvh_build.cu). Synchronous: the share size comes back to
 // the host (*count_out) before the share is sorted.

@@ -126,6 +126,45 @@ def _owned_queries_cuda(handle, queries: torch.Tensor, rank: int, world: int, sp
                          _split_chunk(m, world, split))
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    """One extra stream per device for work that runs beside the build."""
+    key = torch.device(device).index
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(device=device)
+    return _SIDE_STREAMS[key]
+
+
+def _build_and_share(points: torch.Tensor, queries: torch.Tensor, rank: int, world: int, split: str):
+    """The BVH of `points` (built on the current stream) and this rank's share of
+    the queries, selected at the same time on a side stream: the share needs only
+    the scene box, which tbvh_scene_bounds gives bit-identical to the build's, so
+    the selection overlaps the build's sort and tree kernels. The current stream
+    waits for the share before anything after this call. Returns (bvh, share)."""
+    from ._bvh_class import BVH
+    from ._native import scene_bounds, share_queries
+
+    main = torch.cuda.current_stream(points.device)
+    ready = torch.cuda.Event()
+    ready.record(main)
+    bvh = BVH(points)
+    _phase("build", queries.device)
+    m = queries.shape[0]
+    if split == "contiguous":
+        q0, q1 = shard_range(m, world, rank)
+        return bvh, torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
+    side = _side_stream(points.device)
+    side.wait_event(ready)
+    with torch.cuda.stream(side):
+        lo, hi = scene_bounds(points)
+        share = share_queries(queries, lo, hi, rank, world, _split_chunk(m, world, split))
+    main.wait_stream(side)
+    share.record_stream(main)
+    return bvh, share
+
+
 class PeerResults:
     """(M, k) result buffers on every rank of `group`, each mapped on every other
     rank through CUDA IPC, for ``knn_sharded_single_cloud(..., gather="all", out=...)``.
@@ -224,13 +263,11 @@ def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, rank: i
                     out: PeerResults):
     """One BVH build; this rank's share of the queries; results delivered to
     every rank's `out`."""
-    from ._bvh_class import BVH
     from ._native import query_knn_share
 
-    with BVH(points) as bvh:
+    bvh, share = _build_and_share(points, queries, rank, world, split)
+    with bvh:
         h = bvh._handle
-        _phase("build", queries.device)
-        share = _owned_queries_cuda(h, queries, rank, world, split)
         # No rank may store into a peer's buffers while that peer still reads the
         # previous call's rows: a collective on every rank's current stream, after
         # its earlier reads and before any traversal, orders them.
@@ -299,10 +336,8 @@ def knn_sharded_single_cloud(points: torch.Tensor | None, queries: torch.Tensor,
         idx, dist_sq = knn_fn(buf, queries[q0:q1].contiguous(), k)
         owned = torch.arange(q0, q1, dtype=torch.int64, device=queries.device)
     elif order_fn is None and knn_fn is default_knn:
-        from ._bvh_class import BVH
-
-        with BVH(buf) as bvh:
-            owned = _owned_queries_cuda(bvh._handle, queries, rank, world, split)
+        bvh, owned = _build_and_share(buf, queries, rank, world, split)
+        with bvh:
             idx, dist_sq = bvh.knn(queries.index_select(0, owned), k, sort_queries=False)
     else:
         order = order_fn(buf, queries) if order_fn is not None else _full_morton_order(buf, queries)
