@@ -90,6 +90,9 @@ def _worker(rank, world, port, outdir, mode):
         out["morton_none"] = tdist.knn_sharded_single_cloud(sp if rank == 0 else None, sq, 4, num_points=700, dim=3,
                                                             gather="none", order_fn=oracle_order, knn_fn=oracle_knn)
         out["batched"] = tdist.knn_sharded_batched(bp, bq, 4, knn_fn=oracle_knn)
+        # An even split: every rank's block has the same length (gathered in place).
+        out["batched_even"] = tdist.knn_sharded_batched(bp[:4].contiguous(), bq[:4].contiguous(), 4,
+                                                        knn_fn=oracle_knn)
         out["ragged"] = tdist.knn_sharded_ragged(rp, bo, rq, qo, 4, knn_fn=oracle_knn)
         torch.save(out, Path(outdir) / f"rank{rank}.pt")
         dist.destroy_process_group()
@@ -160,6 +163,7 @@ def test_sharded_paths_match_single_process():
     ri, rd = oracle_knn(rp, rq, 4, batch_offsets=torch.tensor(bo), query_offsets=torch.tensor(qo))
     for r in (r0, r1):
         assert torch.equal(r["batched"][0], bi) and torch.equal(r["batched"][1], bd)
+        assert torch.equal(r["batched_even"][0], bi[:4]) and torch.equal(r["batched_even"][1], bd[:4])
         assert torch.equal(r["ragged"][0], ri) and torch.equal(r["ragged"][1], rd)
 
 

@@ -88,6 +88,8 @@ def _worker(rank, world, port, outdir):
             peer.close()
         i, d = tdist.knn_sharded_batched(bp.to(dev), bq.to(dev), 8)
         out["batched"] = (i.cpu(), d.cpu())
+        i, d = tdist.knn_sharded_batched(bp[:4].to(dev), bq[:4].to(dev), 8)  # equal blocks on 1, 2 and 4 ranks
+        out["batched_even"] = (i.cpu(), d.cpu())
         i, d = tdist.knn_sharded_ragged(rp.to(dev), bo, rq.to(dev), qo, 16)
         out["ragged"] = (i.cpu(), d.cpu())
         torch.cuda.synchronize(dev)
@@ -141,6 +143,7 @@ def test_sharded_knn_matches_one_gpu(world):
                 gi, gd = got[f"peer{bits}_{rep}"]
                 assert torch.equal(gi, wi) and torch.equal(gd, wd)
         assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
+        assert torch.equal(got["batched_even"][0], bi[:4].cpu()) and torch.equal(got["batched_even"][1], bd[:4].cpu())
         assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())
     shares = [torch.load(Path(outdir) / f"rank{r}.pt")["single_none"][2] for r in range(world)]
     owned = torch.cat(shares)

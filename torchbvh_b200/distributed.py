@@ -69,15 +69,20 @@ def _world(group) -> tuple[int, int]:
 
 
 def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Tensor:
-    """All-gathers row blocks of different lengths (padded to the longest) and concatenates them."""
+    """Every rank's row block, concatenated in rank order. Equal blocks are
+    gathered straight into the result (one collective, no copies); blocks of
+    different lengths are padded to the longest and compacted afterwards."""
     world, _ = _world(group)
     width = tuple(local.shape[1:])
     longest = max(counts)
+    gathered = torch.empty((longest * world, *width), dtype=local.dtype, device=local.device)
+    if all(c == longest for c in counts):
+        dist.all_gather_into_tensor(gathered, local.contiguous(), group=group)
+        return gathered
     padded = torch.zeros((longest, *width), dtype=local.dtype, device=local.device)
     padded[: local.shape[0]] = local
-    bufs = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(bufs, padded, group=group)
-    return torch.cat([b[:c] for b, c in zip(bufs, counts)])
+    dist.all_gather_into_tensor(gathered, padded, group=group)
+    return torch.cat([gathered[r * longest: r * longest + c] for r, c in enumerate(counts)])
 
 
 SPLITS = ("morton", "interleaved", "contiguous")
