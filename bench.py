@@ -74,6 +74,9 @@ def parse_args():
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
     ap.add_argument("--c4-index-bits", type=int, default=32, choices=[32, 64],
                     help="c4 on N > 1 GPUs: width of the indices the traversal sends over NVLink")
+    ap.add_argument("--c4-transport", default="auto", choices=["auto", "multicast", "peer"],
+                    help="c4 on N > 1 GPUs: rows to every rank through one NVLink multicast store (where "
+                         "supported) or one store per peer")
     ap.add_argument("--c4-split", default="morton", choices=["morton", "interleaved", "contiguous"],
                     help="c4 on N > 1 GPUs: share of the queries per rank (one range of their Morton order, "
                          "runs of it dealt to the ranks in turn, or a range of their given order)")
@@ -591,7 +594,9 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
         ev.record(torch.cuda.current_stream(dev))
         phase_events.append((name, ev))
 
-    with tdist.PeerResults(m, k, device=device, index_bits=args.c4_index_bits) as peer:
+    with tdist.PeerResults(m, k, device=device, index_bits=args.c4_index_bits,
+                           transport=args.c4_transport) as peer:
+        transport_used = peer.transport_used
         _native._knn_hooks.append(hook)
         tdist._phase_hooks.append(phase_hook)
         sampler = ClockSampler(local)
@@ -680,7 +685,9 @@ def run_b200_single_cloud_sharded(args, world, rank, local):
                    "parallelism": (f"points broadcast from rank 0 (NCCL), BVH built on each of {world} GPUs, "
                                    f"queries split by {'Morton-order' if args.c4_split == 'morton' else 'index'} "
                                    f"range, every result row delivered to every rank by the traversal "
-                                   f"(NVLink stores): results all-gathered")},
+                                   f"({'one NVLink multicast store per row' if transport_used == 'multicast' else 'NVLink stores to every peer'}, "
+                                   f"int{args.c4_index_bits} indices on the wire): results all-gathered"),
+                   "transport": transport_used, "index_bits": args.c4_index_bits},
         "results_in_place": {"value": m * gather_steps / (inplace_ms / 1e3), "unit": UNIT,
                              "ms_per_step": inplace_ms / gather_steps,
                              "note": "same step with each result row left on the rank that computed it"},

@@ -254,6 +254,23 @@ int tbvh_query_knn_share_i32(int device, const float* node_aabbs, const int64_t*
                              int dim, int k, int num_dest, int32_t* const* dest_indices,
                              float* const* dest_distances, void* stream);
 
+/* tbvh_query_knn_share_i32 with one pair of multicast destinations: mc_indices
+ * (int32 [num_queries, k]) and mc_distances (float32 [num_queries, k]) are
+ * addresses in a CUDA multicast object (cuMulticastCreate / cuMulticastBindMem,
+ * mapped on this device; e.g. the multicast_ptr of a PyTorch symmetric-memory
+ * buffer) with every rank's buffer bound to it. Each finished row is written
+ * with 16-byte multimem.st stores: it leaves this GPU once and the NVLink
+ * switch delivers it to every bound buffer, the local one included, instead of
+ * one NVLink store per peer. Addresses must be 16-byte aligned and must be
+ * multicast addresses (a plain device pointer is not valid for these stores).
+ * Ordering as for tbvh_query_knn_share (system-scope fence at the end of the
+ * kernel; a collective after it on every rank before reads). No reference
+ * counterpart. */
+int tbvh_query_knn_share_multicast(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                                   int64_t num_points, const float* queries, int64_t num_queries,
+                                   const int64_t* order, int64_t share_count, int dim, int k,
+                                   int32_t* mc_indices, float* mc_distances, void* stream);
+
 /* dst[i] = src[i] (int32 -> int64) for i < count, on `stream`. No reference counterpart. */
 int tbvh_widen_indices(int device, const int32_t* src, int64_t* dst, int64_t count, void* stream);
 

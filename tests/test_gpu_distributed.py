@@ -51,6 +51,9 @@ def _peer_query_sets(big_q):
     return [big_q, big_q.flip(0).contiguous(), torch.rand(big_q.shape, generator=g)]
 
 
+_PEER_FORMS = ((32, "auto"), (32, "peer"), (64, "peer"))
+
+
 def _worker(rank, world, port, outdir):
     import datetime
 
@@ -78,13 +81,15 @@ def _worker(rank, world, port, outdir):
         # Fused all-gather: each rank's traversal writes its rows into every
         # rank's buffers over NVLink (int32 or int64 indices on the wire); the
         # same buffers serve consecutive calls.
-        for bits in (32, 64):
-            peer = tdist.PeerResults(big_q.shape[0], 32, device=dev, index_bits=bits)
+        # "auto" takes the NVLink multicast transport where the devices support it.
+        for bits, transport in _PEER_FORMS:
+            peer = tdist.PeerResults(big_q.shape[0], 32, device=dev, index_bits=bits, transport=transport)
+            out[f"transport{bits}{transport}"] = peer.transport_used
             for rep, (split, qset) in enumerate(zip(("morton", "morton", "contiguous"), _peer_query_sets(big_q))):
                 i, d = tdist.knn_sharded_single_cloud(big_p.to(dev) if rank == 0 else None, qset.to(dev), 32,
                                                       num_points=big_p.shape[0], dim=3, device=dev, split=split,
                                                       out=peer)
-                out[f"peer{bits}_{rep}"] = (i.cpu().clone(), d.cpu().clone())
+                out[f"peer{bits}{transport}_{rep}"] = (i.cpu().clone(), d.cpu().clone())
             peer.close()
         i, d = tdist.knn_sharded_batched(bp.to(dev), bq.to(dev), 8)
         out["batched"] = (i.cpu(), d.cpu())
@@ -137,11 +142,12 @@ def test_sharded_knn_matches_one_gpu(world):
         assert torch.equal(got["single_contiguous"][1], sd.cpu())
         i, d, rows = got["single_none"]
         assert torch.equal(i, si.cpu()[rows]) and torch.equal(d, sd.cpu()[rows])
-        for bits in (32, 64):
+        for bits, transport in _PEER_FORMS:
+            assert got[f"transport{bits}{transport}"] in (("multicast", "peer") if transport == "auto" else (transport,))
             for rep in range(3):
                 wi, wd = peer_want[rep]
-                gi, gd = got[f"peer{bits}_{rep}"]
-                assert torch.equal(gi, wi) and torch.equal(gd, wd)
+                gi, gd = got[f"peer{bits}{transport}_{rep}"]
+                assert torch.equal(gi, wi) and torch.equal(gd, wd), (bits, transport, rep)
         assert torch.equal(got["batched"][0], bi.cpu()) and torch.equal(got["batched"][1], bd.cpu())
         assert torch.equal(got["batched_even"][0], bi[:4].cpu()) and torch.equal(got["batched_even"][1], bd[:4].cpu())
         assert torch.equal(got["ragged"][0], ri.cpu()) and torch.equal(got["ragged"][1], rd.cpu())

@@ -86,6 +86,9 @@ _SIGNATURES = {
         [_i32, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i32, _i32, _i32, ctypes.POINTER(_ptr),
          ctypes.POINTER(_ptr), _ptr],
     ),
+    "tbvh_query_knn_share_multicast": (
+        _i32, [_i32, _ptr, _ptr, _i64, _ptr, _i64, _ptr, _i64, _i32, _i32, _ptr, _ptr, _ptr],
+    ),
     "tbvh_widen_indices": (_i32, [_i32, _ptr, _ptr, _i64, _ptr]),
     "tbvh_query_knn_gather": (
         _i32,
@@ -582,10 +585,12 @@ def widen_indices(src: torch.Tensor, dst: torch.Tensor) -> None:
 
 def query_knn_share(node_aabbs: torch.Tensor, sorted_indices: torch.Tensor, num_points: int,
                     queries: torch.Tensor, share: torch.Tensor, k: int,
-                    dest_indices: list[int], dest_distances: list[int], index_bits: int = 64) -> None:
+                    dest_indices: list[int], dest_distances: list[int], index_bits: int = 64,
+                    multicast: bool = False) -> None:
     """k-NN of the queries listed in `share` (int64 indices into `queries`), each result
     row written at the query's row of every destination buffer (tbvh_query_knn_share;
-    index_bits = 32: int32 destination index buffers, tbvh_query_knn_share_i32)."""
+    index_bits = 32: int32 destination index buffers, tbvh_query_knn_share_i32;
+    multicast: one pair of multicast addresses, tbvh_query_knn_share_multicast)."""
     op = "query_knn_share"
     if not (queries.is_cuda and queries.is_contiguous() and queries.dtype == torch.float32 and queries.dim() == 2):
         raise RuntimeError(f"{op}: queries must be contiguous CUDA float32 (M, D)")
@@ -604,12 +609,21 @@ def query_knn_share(node_aabbs: torch.Tensor, sorted_indices: torch.Tensor, num_
             h("start", device)
     if index_bits not in (32, 64):
         raise RuntimeError(f"{op}: index_bits must be 32 or 64")
-    entry = lib.tbvh_query_knn_share_i32 if index_bits == 32 else lib.tbvh_query_knn_share
-    _check(entry(
-        device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), int(num_points), queries.data_ptr(),
-        int(queries.size(0)), share.data_ptr(), int(share.numel()), int(queries.size(1)), int(k), n_dest,
-        idx_arr, dist_arr, _stream(device),
-    ))
+    if multicast:
+        if n_dest != 1 or index_bits != 32:
+            raise RuntimeError(f"{op}: multicast takes one pair of addresses and int32 indices")
+        _check(lib.tbvh_query_knn_share_multicast(
+            device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), int(num_points), queries.data_ptr(),
+            int(queries.size(0)), share.data_ptr(), int(share.numel()), int(queries.size(1)), int(k),
+            dest_indices[0], dest_distances[0], _stream(device),
+        ))
+    else:
+        entry = lib.tbvh_query_knn_share_i32 if index_bits == 32 else lib.tbvh_query_knn_share
+        _check(entry(
+            device.index, node_aabbs.data_ptr(), sorted_indices.data_ptr(), int(num_points), queries.data_ptr(),
+            int(queries.size(0)), share.data_ptr(), int(share.numel()), int(queries.size(1)), int(k), n_dest,
+            idx_arr, dist_arr, _stream(device),
+        ))
     if hooks:
         for h in hooks:
             h("end", device)

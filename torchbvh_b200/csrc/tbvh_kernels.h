@@ -156,6 +156,9 @@ struct KnnLaunch {
   // buffers of other GPUs (NVLink stores).
   int num_dest = 0;
   bool dest_idx32 = false;  // dest_idx buffers hold int32 indices (the caller widens them)
+  // dest_idx[0] / dest_dist[0] are multicast addresses (num_dest == 1, int32
+  // indices): one multimem store per 16 bytes reaches every GPU of the group.
+  bool dest_multimem = false;
   int64_t* dest_idx[kMaxDest] = {};
   float* dest_dist[kMaxDest] = {};
 };

@@ -151,6 +151,7 @@ struct KnnArgs {
   int spatial;              // 1: write row = sorted (Morton) position, else the query's own row
   int num_dest;             // > 0: rows go to dest_* (row = query index) instead of out_*
   int dest_idx32;           // 1: dest_idx buffers hold int32 indices
+  int dest_multimem;        // 1: dest_idx[0] / dest_dist[0] are multicast addresses (int32 indices)
   int64_t* dest_idx[kMaxDest];
   float* dest_dist[kMaxDest];
   unsigned* status;
@@ -433,6 +434,47 @@ __device__ __forceinline__ void write_rows_coop(const KnnArgs& a, const u64* hw,
         a.out_idx[at] = key_idx(key);
         a.out_dist[at] = key_dist(key);
       }
+    }
+  }
+}
+
+// One 16-byte store through a multicast address: the NVLink switch delivers it
+// to the same offset of the buffer bound on every GPU of the multicast group
+// (local GPU included). A row sent this way leaves the GPU once, whatever the
+// number of GPUs.
+__device__ __forceinline__ void multimem_store4(void* addr, float a, float b, float c, float d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+               :: "l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// Result rows of a warp whose heaps are sorted, to multicast destinations
+// (int32 indices): lane l writes slots 4·(l mod K/4) .. +3 of one row, one
+// 16-byte store per array, so a warp instruction carries 128 / K rows.
+template <int K>
+__device__ __forceinline__ void write_rows_multimem(const KnnArgs& a, const u64* hw, unsigned mask,
+                                                    int64_t row_of_lane, unsigned lane) {
+  constexpr int kLanesPerRow = K / 4;
+  constexpr int kRowsPerPass = 32 / kLanesPerRow;
+  const int sub = int(lane) / kLanesPerRow;
+  const int s0 = (int(lane) % kLanesPerRow) * 4;
+  int32_t* idx = reinterpret_cast<int32_t*>(a.dest_idx[0]);
+  float* dst = a.dest_dist[0];
+  while (mask) {
+    int j = -1;
+#pragma unroll
+    for (int r = 0; r < kRowsPerPass; ++r) {
+      const int next = mask ? __ffs(mask) - 1 : -1;
+      if (r == sub) j = next;
+      if (mask) mask &= mask - 1u;
+    }
+    const int64_t row = __shfl_sync(kFullMask, row_of_lane, j < 0 ? 0 : j);
+    if (j >= 0) {
+      const u64 k0 = hw[heap_word(s0, unsigned(j))], k1 = hw[heap_word(s0 + 1, unsigned(j))];
+      const u64 k2 = hw[heap_word(s0 + 2, unsigned(j))], k3 = hw[heap_word(s0 + 3, unsigned(j))];
+      const int64_t at = row * K + s0;
+      multimem_store4(idx + at, __int_as_float(key_idx(k0)), __int_as_float(key_idx(k1)),
+                      __int_as_float(key_idx(k2)), __int_as_float(key_idx(k3)));
+      multimem_store4(dst + at, key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
     }
   }
 }
@@ -877,7 +919,11 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
     // NVLink, the peers' copies) are then whole-row stores.
     __syncwarp();
     const int64_t row = kToDest ? gq : (a.spatial ? pos : gq);
-    write_rows_coop<K, kToDest>(a, top.hw, __ballot_sync(kFullMask, mine), row, lane);
+    if (kToDest && a.dest_multimem) {
+      write_rows_multimem<K>(a, top.hw, __ballot_sync(kFullMask, mine), row, lane);
+    } else {
+      write_rows_coop<K, kToDest>(a, top.hw, __ballot_sync(kFullMask, mine), row, lane);
+    }
     if constexpr (!kToDest) {
       if (mine && a.out_pos) {
         // Fused source_points[indices] gather (see below for the rule on -1).
@@ -907,6 +953,12 @@ __device__ __forceinline__ void search_cloud(const KnnArgs& a, KnnSmem<K>& s, in
       const longlong2 i01 = make_longlong2(key_idx(k0), key_idx(k1));
       const longlong2 i23 = make_longlong2(key_idx(k2), key_idx(k3));
       const float4 d4 = make_float4(key_dist(k0), key_dist(k1), key_dist(k2), key_dist(k3));
+      if (a.dest_multimem) {
+        multimem_store4(reinterpret_cast<int32_t*>(a.dest_idx[0]) + gq * K + i, __int_as_float(key_idx(k0)),
+                        __int_as_float(key_idx(k1)), __int_as_float(key_idx(k2)), __int_as_float(key_idx(k3)));
+        multimem_store4(a.dest_dist[0] + gq * K + i, d4.x, d4.y, d4.z, d4.w);
+        continue;
+      }
 #pragma unroll 1
       for (int dst = 0; dst < a.num_dest; ++dst) {
         if (a.dest_idx32) {
@@ -1054,6 +1106,7 @@ cudaError_t launch_knn(const KnnLaunch& q, cudaStream_t stream) {
   a.spatial = q.spatial ? 1 : 0;
   a.num_dest = q.num_dest;
   a.dest_idx32 = q.dest_idx32 ? 1 : 0;
+  a.dest_multimem = q.dest_multimem ? 1 : 0;
   for (int i = 0; i < kMaxDest; ++i) {
     a.dest_idx[i] = q.dest_idx[i];
     a.dest_dist[i] = q.dest_dist[i];

@@ -142,7 +142,7 @@ namespace {
 int share_impl(const char* op, int device, const float* node_aabbs, const int64_t* sorted_indices,
                int64_t num_points, const float* queries, int64_t num_queries, const int64_t* order,
                int64_t share_count, int dim, int k, int num_dest, void* const* dest_indices,
-               float* const* dest_distances, bool idx32, void* stream) {
+               float* const* dest_distances, bool idx32, void* stream, bool multimem = false) {
   tbvh::record_error(TBVH_OK, "");
   if (dim != 2 && dim != 3) return peer_fail(TBVH_ERR_BAD_ARG, op, "D must be 2 or 3");
   if (k != 4 && k != 8 && k != 16 && k != 32)
@@ -159,6 +159,9 @@ int share_impl(const char* op, int device, const float* node_aabbs, const int64_
   if (!dest_indices || !dest_distances) return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL destination list");
   for (int i = 0; i < num_dest; ++i)
     if (!dest_indices[i] || !dest_distances[i]) return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL destination buffer");
+  if (multimem && (num_dest != 1 || !idx32 || reinterpret_cast<uintptr_t>(dest_indices[0]) % 16 != 0 ||
+                   reinterpret_cast<uintptr_t>(dest_distances[0]) % 16 != 0))
+    return peer_fail(TBVH_ERR_BAD_ARG, op, "multicast destinations: one pair of 16-byte aligned addresses");
   if (share_count == 0) return TBVH_OK;
   if (!node_aabbs || !sorted_indices || !queries || !order)
     return peer_fail(TBVH_ERR_BAD_ARG, op, "NULL input pointer");
@@ -184,6 +187,7 @@ int share_impl(const char* op, int device, const float* node_aabbs, const int64_
   q.k = k;
   q.num_dest = num_dest;
   q.dest_idx32 = idx32;
+  q.dest_multimem = multimem;
   for (int i = 0; i < num_dest; ++i) {
     q.dest_idx[i] = static_cast<int64_t*>(dest_indices[i]);
     q.dest_dist[i] = dest_distances[i];
@@ -231,6 +235,16 @@ int tbvh_query_knn_share_i32(int device, const float* node_aabbs, const int64_t*
   return share_impl("query_knn_share_i32", device, node_aabbs, sorted_indices, num_points, queries, num_queries,
                     order, share_count, dim, k, num_dest, reinterpret_cast<void* const*>(dest_indices),
                     dest_distances, true, stream);
+}
+
+int tbvh_query_knn_share_multicast(int device, const float* node_aabbs, const int64_t* sorted_indices,
+                                   int64_t num_points, const float* queries, int64_t num_queries,
+                                   const int64_t* order, int64_t share_count, int dim, int k,
+                                   int32_t* mc_indices, float* mc_distances, void* stream) {
+  void* idx[1] = {mc_indices};
+  float* dst[1] = {mc_distances};
+  return share_impl("query_knn_share_multicast", device, node_aabbs, sorted_indices, num_points, queries,
+                    num_queries, order, share_count, dim, k, 1, idx, dst, true, stream, /*multimem=*/true);
 }
 
 int tbvh_widen_indices(int device, const int32_t* src, int64_t* dst, int64_t count, void* stream) {

@@ -189,19 +189,43 @@ class PeerResults:
     bytes per neighbour; point counts are below 2^31) into a shared int32
     buffer, and each rank widens its copy into the int64 ``indices`` tensor
     after the rows have arrived. ``index_bits=64`` writes int64 directly.
+
+    ``transport``: "peer" maps every rank's buffers on every other rank (CUDA
+    IPC) and the traversal stores each row once per rank; "multicast" binds
+    every rank's buffer to one NVLink multicast object (PyTorch symmetric
+    memory) and the traversal stores each row once, through the multicast
+    address, for the switch to deliver to all ranks (int32 indices only);
+    "auto" (default) takes multicast when every rank's device supports it and
+    index_bits is 32, else peer. ``transport_used`` says which one is in use.
     """
 
     def __init__(self, num_queries: int, k: int, *, group=None, device: torch.device | None = None,
-                 index_bits: int = 32):
+                 index_bits: int = 32, transport: str = "auto"):
         from . import _native
 
         if index_bits not in (32, 64):
             raise ValueError("PeerResults: index_bits must be 32 or 64")
+        if transport not in ("auto", "multicast", "peer"):
+            raise ValueError("PeerResults: transport must be 'auto', 'multicast' or 'peer'")
+        if transport == "multicast" and index_bits != 32:
+            raise ValueError("PeerResults: the multicast transport carries int32 indices (index_bits=32)")
         self.group = group
         self.world, self.rank = _world(group)
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self.num_queries, self.k = int(num_queries), int(k)
         self.index_bits = index_bits
+        self.closed = False
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._opened: list[int] = []
+        self._own: list = []
+        self._symm = None
+        shape = (self.num_queries, self.k)
+        if transport != "peer" and index_bits == 32 and self._open_multicast(shape):
+            self.transport_used = "multicast"
+            return
+        if transport == "multicast":
+            raise RuntimeError("PeerResults: NVLink multicast is not available on every rank")
+        self.transport_used = "peer"
         dev = self.device.index
         rows = max(self.num_queries, 1) * self.k
         self._own = [_native.peer_alloc(dev, rows * index_bits // 8), _native.peer_alloc(dev, rows * 4)]
@@ -227,8 +251,43 @@ class PeerResults:
             self._wire_indices = _native.device_tensor(self._own[0][0], shape, torch.int32, self.device)
             self.indices = torch.empty(shape, dtype=torch.int64, device=self.device)
         self.distances = _native.device_tensor(self._own[1][0], shape, torch.float32, self.device)
-        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.closed = False
+
+    def _open_multicast(self, shape: tuple) -> bool:
+        """One symmetric-memory buffer per rank (int32 indices, then float32
+        distances), all bound to one multicast object. A collective; every rank
+        reaches the same answer."""
+        from torch.distributed import _symmetric_memory as symm_mem
+        from torch._C._distributed_c10d import _SymmetricMemory
+
+        ok = self.world > 1
+        if ok:
+            try:
+                ok = bool(_SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA, self.device.index))
+            except Exception:
+                ok = False
+        if not self._all_ranks(ok):
+            return False
+        rows = max(self.num_queries, 1) * self.k
+        buf = symm_mem.empty(2 * rows, dtype=torch.int32, device=self.device)
+        handle = symm_mem.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        mc = int(handle.multicast_ptr)
+        if not self._all_ranks(mc != 0):
+            del handle, buf
+            return False
+        # The multicast address of this tensor: same offset as in the local buffer.
+        at = mc + (buf.data_ptr() - int(handle.buffer_ptrs[handle.rank]))
+        self._symm = (buf, handle)
+        self.dest_indices = [at]
+        self.dest_distances = [at + rows * 4]
+        self._wire_indices = buf[:rows].view(-1)[: shape[0] * shape[1]].view(shape)
+        self.distances = buf[rows:].view(torch.float32)[: shape[0] * shape[1]].view(shape)
+        self.indices = torch.empty(shape, dtype=torch.int64, device=self.device)
+        return True
+
+    def _all_ranks(self, ok: bool) -> bool:
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(flag.item())
 
     def delivered(self) -> None:
         """Collective on the current stream after the writing launches: once it
@@ -251,10 +310,12 @@ class PeerResults:
         dist.barrier(group=self.group)
         for p in self._opened:
             _native.peer_close(self.device.index, p)
+        self.indices = self.distances = self._wire_indices = None
+        self._symm = None  # every rank releases its multicast binding after the barrier above
+        torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         for p, _ in self._own:
             _native.peer_free(self.device.index, p)
-        self.indices = self.distances = self._wire_indices = None
         self.closed = True
 
     def __enter__(self) -> "PeerResults":
@@ -279,7 +340,8 @@ def _share_to_peers(points: torch.Tensor, queries: torch.Tensor, k: int, rank: i
         out.delivered()
         _phase("share", queries.device)
         query_knn_share(h["node_aabbs"], h["sorted_indices"], points.shape[0], queries, share, k,
-                        out.dest_indices, out.dest_distances, index_bits=out.index_bits)
+                        out.dest_indices, out.dest_distances, index_bits=out.index_bits,
+                        multicast=out.transport_used == "multicast")
     _phase("traversal", queries.device)
     out.delivered()
     out._widen()
