@@ -479,6 +479,13 @@ def run_b200_clouds_sharded(args, world, rank, local):
         form = "knn_sharded_batched: contiguous cloud ranges"
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
+    phase_events: list = []
+
+    def phase_hook(name, dev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        phase_events.append((name, ev))
+
     out = None
     for _ in range(args.warmup):
         out = step()
@@ -487,6 +494,7 @@ def run_b200_clouds_sharded(args, world, rank, local):
     launches0 = _native.load_library().tbvh_kernel_launch_count()
     ev = []
     sampler = ClockSampler(local)
+    tdist._phase_hooks.append(phase_hook)
     with sampler:
         for _ in range(args.steps):
             flush.zero_()
@@ -497,9 +505,19 @@ def run_b200_clouds_sharded(args, world, rank, local):
             b.record(stream)
             ev.append((a, b))
         torch.cuda.synchronize(device)
+    tdist._phase_hooks.remove(phase_hook)
     del out
     launches = _native.load_library().tbvh_kernel_launch_count() - launches0
     total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev), world)
+    # Per-rank phases: own clouds' build + query, then the all-gather (and reorder).
+    import torch.distributed as dist
+
+    names = ["start", "compute", "gathered"]
+    steps_ev = [phase_events[i:i + 3] for i in range(0, len(phase_events), 3)]
+    phases = {f"{b}_ms": sum(st[i][1].elapsed_time(st[i + 1][1]) for st in steps_ev) / len(steps_ev)
+              for i, b in enumerate(names[1:])}
+    per_rank = [None] * world
+    dist.all_gather_object(per_rank, {"step_ms": sum(a.elapsed_time(b) for a, b in ev) / args.steps, **phases})
     cfg = workload_config(w, world)
     cfg["parallelism"] = (f"{form} over {world} GPUs, every result row all-gathered (NCCL) into the "
                           f"original order on every rank")
@@ -517,6 +535,7 @@ def run_b200_clouds_sharded(args, world, rank, local):
         "dtype": "f32",
         "data": "synthetic (seeded CPU generator, torchbvh_b200.workloads)",
         "config": cfg,
+        "per_rank_ms": per_rank,
         "roofline": None,
         "cpu_baseline": None,
         "e2e": None,

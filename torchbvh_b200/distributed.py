@@ -472,13 +472,17 @@ def knn_sharded_batched(points: torch.Tensor, queries: torch.Tensor, k: int, *, 
     b = points.shape[0]
     c0, c1 = shard_range(b, world, rank)
     m = queries.shape[1]
+    _phase("start", queries.device)
     if c1 > c0:
         idx, dist_sq = knn_fn(points[c0:c1].contiguous(), queries[c0:c1].contiguous(), k)
     else:
         idx = torch.empty((0, m, k), dtype=torch.int64, device=queries.device)
         dist_sq = torch.empty((0, m, k), dtype=torch.float32, device=queries.device)
+    _phase("compute", queries.device)
     counts = [shard_range(b, world, r)[1] - shard_range(b, world, r)[0] for r in range(world)]
-    return _all_gather_rows(idx, counts, group), _all_gather_rows(dist_sq, counts, group)
+    gathered = _all_gather_rows(idx, counts, group), _all_gather_rows(dist_sq, counts, group)
+    _phase("gathered", queries.device)
+    return gathered
 
 
 def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: torch.Tensor,
@@ -489,6 +493,7 @@ def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: 
     nb = len(batch_offsets) - 1
     sizes = [batch_offsets[c + 1] - batch_offsets[c] for c in range(nb)]
     parts = partition_clouds(sizes, world)
+    _phase("start", queries.device)
     mine = parts[rank]
     dev = queries.device
     if mine:
@@ -506,6 +511,7 @@ def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: 
         idx = torch.empty((0, k), dtype=torch.int64, device=dev)
         dist_sq = torch.empty((0, k), dtype=torch.float32, device=dev)
     qcount = [sum(query_offsets[c + 1] - query_offsets[c] for c in parts[r]) for r in range(world)]
+    _phase("compute", dev)
     all_idx = _all_gather_rows(idx, qcount, group)
     all_dist = _all_gather_rows(dist_sq, qcount, group)
     # Back to the original packed order: gathered row p (clouds rank by rank, each
@@ -517,4 +523,6 @@ def knn_sharded_ragged(points: torch.Tensor, batch_offsets: list[int], queries: 
     total = int(lens.sum())
     owner = torch.repeat_interleave(shift.to(dev), lens.to(dev), output_size=total) + \
         torch.arange(total, dtype=torch.int64, device=dev)
-    return _to_query_order(all_idx, owner), _to_query_order(all_dist, owner)
+    result = _to_query_order(all_idx, owner), _to_query_order(all_dist, owner)
+    _phase("gathered", dev)
+    return result
