@@ -200,3 +200,14 @@ def test_shared_buffer_views_cover_every_wire_dtype():
     for dtype in (torch.int64, torch.int32, torch.float32):
         typestr = _native._TYPESTR[dtype]
         assert int(typestr[2:]) == torch.empty((), dtype=dtype).element_size()
+
+
+def test_peer_results_rejects_bad_options_before_any_collective():
+    from torchbvh_b200 import distributed as tdist
+
+    with pytest.raises(ValueError, match="index_bits"):
+        tdist.PeerResults(10, 4, index_bits=16)
+    with pytest.raises(ValueError, match="transport"):
+        tdist.PeerResults(10, 4, transport="nvshmem")
+    with pytest.raises(ValueError, match="int32 indices"):
+        tdist.PeerResults(10, 4, index_bits=64, transport="multicast")
