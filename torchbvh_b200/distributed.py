@@ -268,9 +268,13 @@ class PeerResults:
         if not self._all_ranks(ok):
             return False
         rows = max(self.num_queries, 1) * self.k
-        buf = symm_mem.empty(2 * rows, dtype=torch.int32, device=self.device)
-        handle = symm_mem.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
-        mc = int(handle.multicast_ptr)
+        try:
+            buf = symm_mem.empty(2 * rows, dtype=torch.int32, device=self.device)
+            handle = symm_mem.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+            mc = int(handle.multicast_ptr)
+        except Exception:  # e.g. no symmetric-memory backend: every rank falls back together
+            buf = handle = None
+            mc = 0
         if not self._all_ranks(mc != 0):
             del handle, buf
             return False
