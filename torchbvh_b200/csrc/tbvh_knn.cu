@@ -261,6 +261,13 @@ struct TopK {
 #ifndef TBVH_KNN_UNROLLED_SIFT
 #define TBVH_KNN_UNROLLED_SIFT 1
 #endif
+// Children per heap node: 2 (binary) or 4 (a sift of a 32-slot heap is then 3
+// dependent levels of four independent loads instead of 5 levels of two).
+#ifndef TBVH_KNN_HEAP_ARITY
+#define TBVH_KNN_HEAP_ARITY 2
+#endif
+constexpr int kArity = TBVH_KNN_HEAP_ARITY;
+static_assert(kArity == 2 || kArity == 4, "heap arity 2 or 4");
 __device__ __forceinline__ int heap_word(int s, unsigned l) {
   return TBVH_KNN_SWIZZLE ? s * 32 + int(l ^ unsigned(s & 31)) : s * 32 + int(l);
 }
@@ -290,14 +297,17 @@ struct TopK<K, true> {
   __device__ __forceinline__ void sift_down(int i, u64 x, int n) {
 #pragma unroll 1
     for (;;) {
-      int c = 2 * i + 1;
+      int c = kArity * i + 1;
       if (c >= n) break;
       u64 a = h[c];
-      if (c + 1 < n) {
-        const u64 b = h[c + 1];
-        if (b > a) {
-          a = b;
-          ++c;
+#pragma unroll
+      for (int d = 1; d < kArity; ++d) {
+        if (c + d < n) {
+          const u64 b = h[c + d];
+          if (b > a) {
+            a = b;
+            c = kArity * i + 1 + d;
+          }
         }
       }
       if (a <= x) break;
@@ -309,7 +319,7 @@ struct TopK<K, true> {
   __device__ __forceinline__ void seed_slot(int i, u64 v) { h[i] = v; }
   __device__ __forceinline__ void seed_done() {  // bottom-up heapify
 #pragma unroll 1
-    for (int i = K / 2 - 1; i >= 0; --i) sift_down(i, h[i], K);
+    for (int i = (K - 2) / kArity; i >= 0; --i) sift_down(i, h[i], K);
     kth = h[0];
   }
   __device__ __forceinline__ void insert(u64 nk) {  // requires nk < kth: replaces the root
@@ -318,24 +328,35 @@ struct TopK<K, true> {
       kth = h[0];
       return;
     }
-    // The sift from the root unrolled over the heap's log2(K) levels, both
-    // children loaded together at each level. The last internal slot (K/2 - 1)
-    // has only a left child; its missing right one reads as key 0, which never
-    // wins (keys are >= 0 and a move needs a child strictly above nk).
-    constexpr int kLevels = K >= 32 ? 5 : K >= 16 ? 4 : K >= 8 ? 3 : 2;
+    // The sift from the root unrolled over the heap's levels, the children of
+    // a level loaded together.
+    // The new root is known without reading it back: the larger child of
+    // the root if the sift moved past level 0, else nk.
+    constexpr int kLevels = kArity == 2 ? (K >= 32 ? 5 : K >= 16 ? 4 : K >= 8 ? 3 : 2)
+                                        : (K >= 32 ? 3 : K >= 16 ? 2 : 2);
     int i = 0;
     bool moving = true;
+    u64 root = nk;
 #pragma unroll
     for (int lvl = 0; lvl < kLevels; ++lvl) {
-      const int c = 2 * i + 1;
+      const int c = kArity * i + 1;
       if (moving && c < K) {
         u64 a = h[c];
-        const u64 b = c + 1 < K ? h[c + 1] : 0ull;
-        const bool right = b > a;
-        a = right ? b : a;
+        int pick = 0;
+#pragma unroll
+        for (int d = 1; d < kArity; ++d) {
+          // A missing child reads as key 0, which never wins (keys are >= 0
+          // and a move needs a child strictly above nk).
+          const u64 b = c + d < K ? h[c + d] : 0ull;
+          if (b > a) {
+            a = b;
+            pick = d;
+          }
+        }
         if (a > nk) {
           h[i] = a;
-          i = c + (right ? 1 : 0);
+          if (lvl == 0) root = a;
+          i = c + pick;
         } else {
           moving = false;
         }
@@ -344,7 +365,7 @@ struct TopK<K, true> {
       }
     }
     h[i] = nk;
-    kth = h[0];
+    kth = root;
   }
   // In-place heap sort: slots end ascending.
   __device__ __forceinline__ void finish() {
