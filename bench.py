@@ -953,6 +953,9 @@ def run_reference_cuda(args, world, rank, local):
     if not (ref_dir / "torchbvh").exists():
         return {"impl": "reference_cuda", "unavailable": "baseline/_ref not installed"}
     sys.path.insert(0, str(ref_dir))
+    # The reference compiles its extension on first use; one built beside the install
+    # (baseline/_ref/torch_ext) is reused instead of rebuilding on the GPU box.
+    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(ref_dir / "torch_ext"))
     try:
         import torchbvh as ref  # noqa: F401
     except Exception as exc:
