@@ -74,9 +74,9 @@ def parse_args():
                     help="points (= queries) of workload c4; smaller values make ncu-sized cases")
     ap.add_argument("--c4-index-bits", type=int, default=32, choices=[32, 64],
                     help="c4 on N > 1 GPUs: width of the indices the traversal sends over NVLink")
-    ap.add_argument("--c4-transport", default="auto", choices=["auto", "multicast", "peer"],
-                    help="c4 on N > 1 GPUs: rows to every rank through one NVLink multicast store (where "
-                         "supported) or one store per peer")
+    ap.add_argument("--c4-transport", default="peer", choices=["peer", "multicast"],
+                    help="c4 on N > 1 GPUs: rows to every rank by one NVLink store per peer (default) or "
+                         "one multicast store per row")
     ap.add_argument("--c4-split", default="morton", choices=["morton", "interleaved", "contiguous"],
                     help="c4 on N > 1 GPUs: share of the queries per rank (one range of their Morton order, "
                          "runs of it dealt to the ranks in turn, or a range of their given order)")
