@@ -170,3 +170,21 @@ def test_share_rejects_null_destination(native_lib):
 
 def test_empty_share_is_a_no_op(native_lib):
     assert _share(native_lib, count=0) == _native.TBVH_OK
+
+
+def test_multicast_share_checks_its_addresses_before_any_cuda_call(native_lib):
+    """tbvh_query_knn_share_multicast takes one pair of 16-byte aligned multicast
+    addresses; misaligned or NULL ones are refused with no CUDA call (no GPU here)."""
+    call = native_lib.tbvh_query_knn_share_multicast
+    args = dict(device=-1, nodes=16, sorted=16, n=64, queries=16, m=16, order=16, count=0, dim=3, k=8)
+
+    def run(idx, dist, count=0):
+        a = dict(args, count=count)
+        return call(a["device"], a["nodes"], a["sorted"], a["n"], a["queries"], a["m"], a["order"], a["count"],
+                    a["dim"], a["k"], idx, dist, None)
+
+    assert run(4096 + 4, 8192) == _native.TBVH_ERR_BAD_ARG
+    assert b"16-byte aligned" in native_lib.tbvh_last_error()
+    assert run(4096, 8192 + 8) == _native.TBVH_ERR_BAD_ARG
+    assert run(None, 8192) == _native.TBVH_ERR_BAD_ARG
+    assert run(4096, 8192) == _native.TBVH_OK  # an empty share launches nothing
